@@ -1,0 +1,372 @@
+// Residual add + RMSNorm / LayerNorm row reductions (a5, a6).
+//
+// Vector path: a row group of 32*wpr threads owns one row; the row stays in
+// registers (<= 64 F32 values per thread), so x and r are read from HBM once
+// and h and y written once: 8 B per element for F16 activations.  Row sums are
+// reduced with warp shuffles (and shared memory across the warps of a group
+// when wpr > 1).  LayerNorm is two-pass over the register-resident row.
+// Scalar path (rows whose byte length is not a multiple of 32, or unaligned
+// pointers): one CTA per row, re-reading the row from L2.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace levo {
+namespace {
+
+constexpr int kThreads = 256;
+
+struct NormArgs {
+    const void *x;
+    const void *r;
+    const float *gamma;
+    const float *beta;
+    void *h_out;
+    void *y_out;
+    int64_t rows;
+    int dim;
+    int wpr;  // warps per row (vector path)
+    float eps;
+    int f16_boundary;
+};
+
+template <typename T>
+struct Act;
+template <>
+struct Act<__half> {
+    static constexpr int kVec = 16;  // elements per 32-byte vector
+    __device__ static float round(float v) { return __half2float(__float2half_rn(v)); }
+    __device__ static void unpack(const u32x8 &w, float *out) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const __half2 h2 = *reinterpret_cast<const __half2 *>(&w.v[i]);
+            const float2 f = __half22float2(h2);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    }
+    __device__ static u32x8 pack(const float *in) {
+        u32x8 w;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const __half2 h2 = __floats2half2_rn(in[2 * i], in[2 * i + 1]);
+            w.v[i] = *reinterpret_cast<const uint32_t *>(&h2);
+        }
+        return w;
+    }
+    __device__ static float load1(const void *p, int64_t i) {
+        return __half2float(static_cast<const __half *>(p)[i]);
+    }
+    __device__ static void store1(void *p, int64_t i, float v) {
+        static_cast<__half *>(p)[i] = __float2half_rn(v);
+    }
+};
+template <>
+struct Act<float> {
+    static constexpr int kVec = 8;
+    __device__ static float round(float v) { return v; }
+    __device__ static void unpack(const u32x8 &w, float *out) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = __uint_as_float(w.v[i]);
+    }
+    __device__ static u32x8 pack(const float *in) {
+        u32x8 w;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w.v[i] = __float_as_uint(in[i]);
+        return w;
+    }
+    __device__ static float load1(const void *p, int64_t i) {
+        return static_cast<const float *>(p)[i];
+    }
+    __device__ static void store1(void *p, int64_t i, float v) {
+        static_cast<float *>(p)[i] = v;
+    }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Sum over the `wpr` warps of a row group.  Every thread of the CTA calls it
+// (the __syncthreads are CTA-wide); `slot` is the group's first warp.
+__device__ __forceinline__ float group_sum(float v, int wpr, float *red) {
+    v = warp_sum(v);
+    if (wpr == 1) return v;
+    const int warp = threadIdx.x >> 5;
+    const int first = (warp / wpr) * wpr;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.f;
+    for (int w = 0; w < wpr; ++w) s += red[first + w];
+    return s;
+}
+
+// Final y value from the normalised value n for column j.
+template <typename T, bool LAYER>
+__device__ __forceinline__ float norm_output(const NormArgs &a, float n, float g, float b) {
+    if (a.f16_boundary) n = Act<T>::round(n);
+    float y = __fmul_rn(n, g);
+    if (LAYER) y = __fadd_rn(y, b);
+    return y;
+}
+
+template <typename T, int VPL, bool LAYER>
+__global__ void __launch_bounds__(kThreads) add_norm_vec_kernel(const NormArgs a) {
+    constexpr int VE = Act<T>::kVec;
+    __shared__ float red[kThreads / 32];
+    const int group_threads = 32 * a.wpr;
+    const int groups = kThreads / group_threads;
+    const int group = threadIdx.x / group_threads;
+    const int gl = threadIdx.x % group_threads;
+    const int nvec = a.dim / VE;
+    const float inv_dim = 1.0f / static_cast<float>(a.dim);
+
+    for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * groups; row0 < a.rows;
+         row0 += static_cast<int64_t>(gridDim.x) * groups) {
+        const int64_t row = row0 + group;
+        const bool active = row < a.rows;
+        const size_t row_off = static_cast<size_t>(row) * a.dim * sizeof(T);
+        // hw holds the row in the activation type: h = x + r is exactly
+        // representable there, so the row costs 8 registers per vector.
+        u32x8 hw[VPL], rw[VPL];
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int vi = k * group_threads + gl;
+            if (active && vi < nvec) {
+                hw[k] = ld8u(static_cast<const char *>(a.x) + row_off + vi * 32);
+                if (a.r) rw[k] = ld8u(static_cast<const char *>(a.r) + row_off + vi * 32);
+            }
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int vi = k * group_threads + gl;
+            if (active && vi < nvec) {
+                float h[VE];
+                Act<T>::unpack(hw[k], h);
+                if (a.r) {
+                    float rv[VE];
+                    Act<T>::unpack(rw[k], rv);
+#pragma unroll
+                    for (int i = 0; i < VE; ++i) h[i] = Act<T>::round(__fadd_rn(h[i], rv[i]));
+                    hw[k] = Act<T>::pack(h);
+                }
+#pragma unroll
+                for (int i = 0; i < VE; ++i) sum += LAYER ? h[i] : h[i] * h[i];
+            }
+        }
+        sum = group_sum(sum, a.wpr, red);
+        float mean = 0.f, scale;
+        if (LAYER) {
+            mean = sum * inv_dim;
+            float sq = 0.f;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const int vi = k * group_threads + gl;
+                if (active && vi < nvec) {
+                    float h[VE];
+                    Act<T>::unpack(hw[k], h);
+#pragma unroll
+                    for (int i = 0; i < VE; ++i) {
+                        const float d = __fsub_rn(h[i], mean);
+                        sq += d * d;
+                    }
+                }
+            }
+            sq = group_sum(sq, a.wpr, red);
+            scale = 1.0f / sqrtf(sq * inv_dim + a.eps);
+        } else {
+            scale = 1.0f / sqrtf(sum * inv_dim + a.eps);
+        }
+        if (!active) continue;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int vi = k * group_threads + gl;
+            if (vi >= nvec) continue;
+            const int col = vi * VE;
+            if (a.h_out && a.r) st8u(static_cast<char *>(a.h_out) + row_off + vi * 32, hw[k]);
+            float h[VE];
+            Act<T>::unpack(hw[k], h);
+#pragma unroll
+            for (int i = 0; i < VE; i += 8) {
+                const f32x8 g = ld8_ro(a.gamma + col + i);
+                f32x8 b{};
+                if (LAYER) b = ld8_ro(a.beta + col + i);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float n = LAYER ? __fmul_rn(__fsub_rn(h[i + j], mean), scale)
+                                          : __fmul_rn(h[i + j], scale);
+                    h[i + j] = norm_output<T, LAYER>(a, n, g.v[j], b.v[j]);
+                }
+            }
+            st8u(static_cast<char *>(a.y_out) + row_off + vi * 32, Act<T>::pack(h));
+        }
+    }
+}
+
+// Fallback: one CTA per row, any dim and alignment.
+template <typename T, bool LAYER>
+__global__ void __launch_bounds__(kThreads) add_norm_scalar_kernel(const NormArgs a) {
+    __shared__ float red[kThreads / 32];
+    const float inv_dim = 1.0f / static_cast<float>(a.dim);
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        const int64_t base = row * a.dim;
+        auto hval = [&](int j) {
+            float v = Act<T>::load1(a.x, base + j);
+            if (a.r) v = Act<T>::round(__fadd_rn(v, Act<T>::load1(a.r, base + j)));
+            return v;
+        };
+        float sum = 0.f;
+        for (int j = threadIdx.x; j < a.dim; j += kThreads) {
+            const float v = hval(j);
+            sum += LAYER ? v : v * v;
+        }
+        __syncthreads();
+        sum = warp_sum(sum);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+        __syncthreads();
+        sum = 0.f;
+        for (int w = 0; w < kThreads / 32; ++w) sum += red[w];
+        float mean = 0.f, scale;
+        if (LAYER) {
+            mean = sum * inv_dim;
+            float sq = 0.f;
+            for (int j = threadIdx.x; j < a.dim; j += kThreads) {
+                const float d = __fsub_rn(hval(j), mean);
+                sq += d * d;
+            }
+            __syncthreads();
+            sq = warp_sum(sq);
+            if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+            __syncthreads();
+            sq = 0.f;
+            for (int w = 0; w < kThreads / 32; ++w) sq += red[w];
+            scale = 1.0f / sqrtf(sq * inv_dim + a.eps);
+        } else {
+            scale = 1.0f / sqrtf(sum * inv_dim + a.eps);
+        }
+        for (int j = threadIdx.x; j < a.dim; j += kThreads) {
+            const float v = hval(j);
+            if (a.h_out && a.r) Act<T>::store1(a.h_out, base + j, v);
+            const float n = LAYER ? __fmul_rn(__fsub_rn(v, mean), scale) : __fmul_rn(v, scale);
+            Act<T>::store1(a.y_out, base + j,
+                           norm_output<T, LAYER>(a, n, a.gamma[j], LAYER ? a.beta[j] : 0.f));
+        }
+    }
+}
+
+template <typename T, int VPL, bool LAYER>
+void launch_vec(const NormArgs &a, cudaStream_t stream) {
+    const int groups = kThreads / (32 * a.wpr);
+    const int64_t grid = std::min<int64_t>((a.rows + groups - 1) / groups,
+                                           static_cast<int64_t>(sm_count()) * 64);
+    add_norm_vec_kernel<T, VPL, LAYER><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(a);
+}
+
+template <typename T, bool LAYER>
+int run_norm(const char *what, const void *x, const void *r, const float *gamma, const float *beta,
+             void *h_out, void *y_out, int64_t rows, int64_t dim, float eps, uint32_t flags,
+             cudaStream_t stream) {
+    clear_error();
+    const std::string w(what);
+    if (x == nullptr || y_out == nullptr || gamma == nullptr || (LAYER && beta == nullptr))
+        return set_error(LEVO_OPS_EINVAL, w + ": required pointer is null");
+    if (rows < 0 || dim < 0) return set_error(LEVO_OPS_EINVAL, w + ": negative shape");
+    if (!(eps >= 0.f) || !std::isfinite(eps))
+        return set_error(LEVO_OPS_EINVAL, w + ": eps must be finite and non-negative");
+    if (flags & ~LEVO_NORM_F16_BOUNDARY) return set_error(LEVO_OPS_EINVAL, w + ": unknown flag bits");
+    if ((flags & LEVO_NORM_F16_BOUNDARY) && sizeof(T) != 2)
+        return set_error(LEVO_OPS_EINVAL, w + ": the F16 boundary flag needs F16 activations");
+    const void *ptrs[6] = {x, r, h_out, y_out, gamma, beta};
+    for (int i = 0; i < 6; ++i)
+        if (ptrs[i] && !aligned_to(ptrs[i], i < 4 ? sizeof(T) : 4))
+            return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
+    if (rows == 0 || dim == 0) return LEVO_OPS_OK;
+    if (dim > (1 << 20)) return set_error(LEVO_OPS_EUNSUPPORTED, w + ": dim above 1048576");
+
+    NormArgs a{x, r, gamma, beta, h_out, y_out, rows, static_cast<int>(dim), 1, eps,
+               (flags & LEVO_NORM_F16_BOUNDARY) ? 1 : 0};
+    constexpr int VE = Act<T>::kVec;
+    constexpr int kMaxVpl = sizeof(T) == 2 ? 4 : 8;  // <= 64 F32 values per thread
+    bool vec = (dim * sizeof(T)) % 32 == 0 && (dim % 8 == 0);
+    for (int i = 0; i < 6 && vec; ++i)
+        if (ptrs[i] && !aligned_to(ptrs[i], 32)) vec = false;
+    int vpl = 0;
+    if (vec) {
+        const int nvec = static_cast<int>(dim / VE);
+        for (int wpr = 1; wpr <= 8; wpr *= 2) {
+            const int need = (nvec + 32 * wpr - 1) / (32 * wpr);
+            if (need <= kMaxVpl) {
+                a.wpr = wpr;
+                vpl = need;
+                break;
+            }
+        }
+        if (vpl == 0) vec = false;
+    }
+    if (vec) {
+        // Instantiated vectors-per-thread: 1,2,3,4 (+6,8 for F32); a larger
+        // count than needed is masked per vector.
+        if (vpl == 1) {
+            launch_vec<T, 1, LAYER>(a, stream);
+        } else if (vpl == 2) {
+            launch_vec<T, 2, LAYER>(a, stream);
+        } else if (vpl == 3) {
+            launch_vec<T, 3, LAYER>(a, stream);
+        } else if (vpl == 4) {
+            launch_vec<T, 4, LAYER>(a, stream);
+        } else if constexpr (sizeof(T) == 4) {
+            if (vpl <= 6) launch_vec<T, 6, LAYER>(a, stream);
+            else launch_vec<T, 8, LAYER>(a, stream);
+        }
+    } else {
+        const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * 8);
+        add_norm_scalar_kernel<T, LAYER><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(a);
+    }
+    return check_launch(what);
+}
+
+}  // namespace
+}  // namespace levo
+
+extern "C" {
+
+LEVO_OPS_API int levo_add_rmsnorm_f16(const void *x, const void *r, const float *gamma, void *h_out,
+                                      void *y_out, int64_t rows, int64_t dim, float eps,
+                                      uint32_t flags, levo_stream_t stream) {
+    return levo::run_norm<__half, false>("levo_add_rmsnorm_f16", x, r, gamma, nullptr, h_out, y_out,
+                                         rows, dim, eps, flags,
+                                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+LEVO_OPS_API int levo_add_rmsnorm_f32(const float *x, const float *r, const float *gamma,
+                                      float *h_out, float *y_out, int64_t rows, int64_t dim,
+                                      float eps, uint32_t flags, levo_stream_t stream) {
+    return levo::run_norm<float, false>("levo_add_rmsnorm_f32", x, r, gamma, nullptr, h_out, y_out,
+                                        rows, dim, eps, flags,
+                                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+LEVO_OPS_API int levo_add_layernorm_f16(const void *x, const void *r, const float *gamma,
+                                        const float *beta, void *h_out, void *y_out, int64_t rows,
+                                        int64_t dim, float eps, uint32_t flags,
+                                        levo_stream_t stream) {
+    return levo::run_norm<__half, true>("levo_add_layernorm_f16", x, r, gamma, beta, h_out, y_out,
+                                        rows, dim, eps, flags,
+                                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+LEVO_OPS_API int levo_add_layernorm_f32(const float *x, const float *r, const float *gamma,
+                                        const float *beta, float *h_out, float *y_out,
+                                        int64_t rows, int64_t dim, float eps, uint32_t flags,
+                                        levo_stream_t stream) {
+    return levo::run_norm<float, true>("levo_add_layernorm_f32", x, r, gamma, beta, h_out, y_out,
+                                       rows, dim, eps, flags,
+                                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,357 @@
+// Streaming elementwise kernels over dense [channels][time] F32 tensors:
+// SnakeBeta (a1), per-channel bias add (a2) and the fused decoder unit (a3).
+//
+// One kernel template serves all three.  Each is a single HBM pass: every
+// input element is read once with a 256-bit load and every output written
+// once with a 256-bit store.  Per-channel parameters (alpha, beta, bias) are
+// promoted to F32, exponentiated and staged in shared memory once per CTA.
+// The grid is persistent (a multiple of the SM count) and walks the flat
+// element space in tiles; a vector that straddles a row boundary selects its
+// parameters per element.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace levo {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 2;
+constexpr int64_t kMaxStagedChannels = 4096;
+
+struct StreamArgs {
+    const float *u;
+    const void *bias;
+    const float *res;
+    const void *alog;
+    const void *blog;
+    float *x_out;
+    float *y_out;
+    int64_t ldu, ldr, ldx, ldy;  // row strides (scalar path only)
+    int64_t rows, len, n;        // n = rows * len
+    int64_t head;                // scalar elements before the 32-byte-aligned region
+    int64_t nvec;                // full 8-element vectors in the aligned region
+    double inv_len;
+    int pdtype;
+    int has_bias, write_x, write_y, tanh_out, staged;
+};
+
+struct ChannelParams {
+    float alpha, beta, bias;
+};
+
+template <bool SNAKE>
+__device__ __forceinline__ ChannelParams channel_params(const StreamArgs &a, const float *smem,
+                                                        int64_t c) {
+    ChannelParams p{0.f, 1.f, 0.f};
+    if (a.staged) {
+        if (SNAKE) {
+            p.alpha = smem[c];
+            p.beta = smem[a.rows + c];
+        }
+        if (a.has_bias) p.bias = smem[2 * a.rows + c];
+    } else {
+        if (SNAKE) {
+            p.alpha = snake_alpha(load_param(a.alog, c, a.pdtype));
+            p.beta = snake_beta_den(load_param(a.blog, c, a.pdtype));
+        }
+        if (a.has_bias) p.bias = load_param(a.bias, c, a.pdtype);
+    }
+    return p;
+}
+
+template <bool HAS_RES, bool SNAKE>
+__device__ __forceinline__ void unit_eval(const StreamArgs &a, const ChannelParams &p, float u,
+                                          float r, float &x, float &y) {
+    float v = u;
+    if (a.has_bias) v = __fadd_rn(v, p.bias);
+    if (HAS_RES) v = __fadd_rn(r, v);
+    x = v;
+    float w = v;
+    if (SNAKE) w = snake_eval(v, p.alpha, p.beta);
+    if (a.tanh_out) w = tanhf(w);
+    y = w;
+}
+
+// Scalar element e with per-tensor row strides.
+template <bool HAS_RES, bool SNAKE>
+__device__ __forceinline__ void scalar_element(const StreamArgs &a, const float *smem, int64_t e) {
+    const int64_t c = row_of(e, a.len, a.inv_len);
+    const int64_t t = e - c * a.len;
+    const ChannelParams p = channel_params<SNAKE>(a, smem, c);
+    const float u = a.u[c * a.ldu + t];
+    const float r = HAS_RES ? a.res[c * a.ldr + t] : 0.f;
+    float x, y;
+    unit_eval<HAS_RES, SNAKE>(a, p, u, r, x, y);
+    if (a.write_x) a.x_out[c * a.ldx + t] = x;
+    if (a.write_y) a.y_out[c * a.ldy + t] = y;
+}
+
+template <bool HAS_RES, bool SNAKE>
+__device__ __forceinline__ void stage_params(const StreamArgs &a, float *smem) {
+    if (!a.staged) return;
+    for (int64_t c = threadIdx.x; c < a.rows; c += blockDim.x) {
+        if (SNAKE) {
+            smem[c] = snake_alpha(load_param(a.alog, c, a.pdtype));
+            smem[a.rows + c] = snake_beta_den(load_param(a.blog, c, a.pdtype));
+        }
+        if (a.has_bias) smem[2 * a.rows + c] = load_param(a.bias, c, a.pdtype);
+    }
+    __syncthreads();
+}
+
+// 256-bit vector path: all tensors dense and sharing one 32-byte phase.
+template <bool HAS_RES, bool SNAKE>
+__global__ void __launch_bounds__(kThreads) stream_vec8_kernel(const StreamArgs a) {
+    extern __shared__ float smem[];
+    stage_params<HAS_RES, SNAKE>(a, smem);
+
+    // Ragged head and tail (< 8 elements each) go to block 0.
+    if (blockIdx.x == 0) {
+        if (threadIdx.x < a.head) scalar_element<HAS_RES, SNAKE>(a, smem, threadIdx.x);
+        const int64_t tail0 = a.head + a.nvec * 8;
+        if (threadIdx.x < a.n - tail0) scalar_element<HAS_RES, SNAKE>(a, smem, tail0 + threadIdx.x);
+    }
+
+    const int64_t tile_vecs = static_cast<int64_t>(kThreads) * kUnroll;
+    for (int64_t tile = static_cast<int64_t>(blockIdx.x) * tile_vecs; tile < a.nvec;
+         tile += static_cast<int64_t>(gridDim.x) * tile_vecs) {
+        f32x8 uu[kUnroll];
+        f32x8 rr[kUnroll];
+#pragma unroll
+        for (int j = 0; j < kUnroll; ++j) {
+            const int64_t vi = tile + j * kThreads + threadIdx.x;
+            if (vi < a.nvec) {
+                const int64_t e = a.head + vi * 8;
+                uu[j] = ld8(a.u + e);
+                if (HAS_RES) rr[j] = ld8(a.res + e);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kUnroll; ++j) {
+            const int64_t vi = tile + j * kThreads + threadIdx.x;
+            if (vi >= a.nvec) continue;
+            const int64_t e = a.head + vi * 8;
+            f32x8 xo, yo;
+            if (a.len >= 8) {
+                // At most one row boundary inside the vector.
+                const int64_t c0 = row_of(e, a.len, a.inv_len);
+                const int64_t boundary = (c0 + 1) * a.len;
+                const ChannelParams p0 = channel_params<SNAKE>(a, smem, c0);
+                if (e + 8 <= boundary) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        unit_eval<HAS_RES, SNAKE>(a, p0, uu[j].v[k], HAS_RES ? rr[j].v[k] : 0.f,
+                                                  xo.v[k], yo.v[k]);
+                } else {
+                    const ChannelParams p1 = channel_params<SNAKE>(a, smem, c0 + 1);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        unit_eval<HAS_RES, SNAKE>(a, (e + k < boundary) ? p0 : p1, uu[j].v[k],
+                                                  HAS_RES ? rr[j].v[k] : 0.f, xo.v[k], yo.v[k]);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const ChannelParams p =
+                        channel_params<SNAKE>(a, smem, row_of(e + k, a.len, a.inv_len));
+                    unit_eval<HAS_RES, SNAKE>(a, p, uu[j].v[k], HAS_RES ? rr[j].v[k] : 0.f,
+                                              xo.v[k], yo.v[k]);
+                }
+            }
+            if (a.write_x) st8(a.x_out + e, xo);
+            if (a.write_y) st8(a.y_out + e, yo);
+        }
+    }
+}
+
+// Scalar path: any row strides, any 4-byte alignment.
+template <bool HAS_RES, bool SNAKE>
+__global__ void __launch_bounds__(kThreads) stream_scalar_kernel(const StreamArgs a) {
+    extern __shared__ float smem[];
+    stage_params<HAS_RES, SNAKE>(a, smem);
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < a.n;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        scalar_element<HAS_RES, SNAKE>(a, smem, e);
+}
+
+template <bool HAS_RES, bool SNAKE>
+int launch_variant(const StreamArgs &a, bool vec, size_t smem_bytes, cudaStream_t stream,
+                   const char *what) {
+    auto kernel = vec ? stream_vec8_kernel<HAS_RES, SNAKE> : stream_scalar_kernel<HAS_RES, SNAKE>;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem_bytes) !=
+            cudaSuccess ||
+        per_sm <= 0)
+        per_sm = 1;
+    const int64_t work_items = vec ? (a.nvec + kUnroll - 1) / kUnroll : a.n;
+    const int64_t needed = std::max<int64_t>(1, (work_items + kThreads - 1) / kThreads);
+    const int64_t grid = std::min<int64_t>(needed, static_cast<int64_t>(sm_count()) * per_sm);
+    kernel<<<static_cast<unsigned>(grid), kThreads, smem_bytes, stream>>>(a);
+    return check_launch(what);
+}
+
+struct StreamRequest {
+    const float *u;
+    int64_t ldu;
+    const void *bias;
+    const float *res;
+    int64_t ldr;
+    const void *alog;
+    const void *blog;
+    int pdtype;
+    float *x_out;
+    int64_t ldx;
+    float *y_out;
+    int64_t ldy;
+    int64_t rows, len;
+    bool tanh_out;
+};
+
+int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
+    const std::string w(what);
+    if (q.rows < 0 || q.len < 0) return set_error(LEVO_OPS_EINVAL, w + ": negative shape");
+    if (q.pdtype != LEVO_DTYPE_F32 && q.pdtype != LEVO_DTYPE_F16)
+        return set_error(LEVO_OPS_EINVAL, w + ": parameter dtype must be F32 or F16");
+    if (q.u == nullptr) return set_error(LEVO_OPS_EINVAL, w + ": input is null");
+    if ((q.alog == nullptr) != (q.blog == nullptr))
+        return set_error(LEVO_OPS_EINVAL, w + ": alpha_log and beta_log must both be given");
+    if (q.x_out == nullptr && q.y_out == nullptr)
+        return set_error(LEVO_OPS_EINVAL, w + ": no output requested");
+    const int64_t lds[4] = {q.ldu, q.res ? q.ldr : q.len, q.x_out ? q.ldx : q.len,
+                            q.y_out ? q.ldy : q.len};
+    for (int64_t ld : lds)
+        if (ld < q.len) return set_error(LEVO_OPS_EINVAL, w + ": row stride smaller than the row");
+    const size_t pbytes = q.pdtype == LEVO_DTYPE_F16 ? 2 : 4;
+    const void *ptrs[7] = {q.u, q.res, q.x_out, q.y_out, q.bias, q.alog, q.blog};
+    for (int i = 0; i < 7; ++i)
+        if (ptrs[i] && !aligned_to(ptrs[i], i < 4 ? 4 : pbytes))
+            return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
+    if (q.rows == 0 || q.len == 0) return LEVO_OPS_OK;
+    if (q.rows > (int64_t(1) << 40) / q.len)
+        return set_error(LEVO_OPS_EINVAL, w + ": tensor too large");
+
+    StreamArgs a{};
+    a.u = q.u;
+    a.bias = q.bias;
+    a.res = q.res;
+    a.alog = q.alog;
+    a.blog = q.blog;
+    a.x_out = q.x_out;
+    a.y_out = q.y_out;
+    a.ldu = q.ldu;
+    a.ldr = q.ldr;
+    a.ldx = q.ldx;
+    a.ldy = q.ldy;
+    a.rows = q.rows;
+    a.len = q.len;
+    a.n = q.rows * q.len;
+    a.inv_len = 1.0 / static_cast<double>(q.len);
+    a.pdtype = q.pdtype;
+    a.has_bias = q.bias != nullptr;
+    a.write_x = q.x_out != nullptr;
+    a.write_y = q.y_out != nullptr;
+    a.tanh_out = q.tanh_out;
+    const bool snake = q.alog != nullptr;
+
+    // The vector path needs dense rows and one common 32-byte phase.
+    bool vec = lds[0] == q.len && lds[1] == q.len && lds[2] == q.len && lds[3] == q.len;
+    const uintptr_t phase = reinterpret_cast<uintptr_t>(q.u) % 32;
+    for (int i = 1; i < 4 && vec; ++i)
+        if (ptrs[i] && reinterpret_cast<uintptr_t>(ptrs[i]) % 32 != phase) vec = false;
+    if (vec) {
+        a.head = std::min<int64_t>(a.n, static_cast<int64_t>(((32 - phase) % 32) / 4));
+        a.nvec = (a.n - a.head) / 8;
+        if (a.nvec == 0) vec = false;
+    }
+
+    const int nparams = (snake ? 2 : 0) + (a.has_bias ? 1 : 0);
+    a.staged = nparams > 0 && q.rows <= kMaxStagedChannels;
+    const size_t smem_bytes = a.staged ? static_cast<size_t>(3 * q.rows) * sizeof(float) : 0;
+
+    if (q.res) {
+        return snake ? launch_variant<true, true>(a, vec, smem_bytes, stream, what)
+                     : launch_variant<true, false>(a, vec, smem_bytes, stream, what);
+    }
+    return snake ? launch_variant<false, true>(a, vec, smem_bytes, stream, what)
+                 : launch_variant<false, false>(a, vec, smem_bytes, stream, what);
+}
+
+}  // namespace
+
+// Used by the chain driver (vae_chain.cu).
+int fused_unit(const levo_fused_unit &unit, cudaStream_t stream) {
+    StreamRequest q{};
+    q.u = unit.u;
+    q.ldu = unit.time;
+    q.bias = unit.bias;
+    q.res = unit.residual;
+    q.ldr = unit.time;
+    q.alog = unit.alpha_log;
+    q.blog = unit.beta_log;
+    q.pdtype = unit.param_dtype;
+    q.x_out = unit.x_out;
+    q.ldx = unit.time;
+    q.y_out = unit.y_out;
+    q.ldy = unit.time;
+    q.rows = unit.channels;
+    q.len = unit.time;
+    q.tanh_out = (unit.flags & LEVO_FUSED_TANH) != 0;
+    if (unit.flags & ~LEVO_FUSED_TANH)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_fused_unit_f32: unknown flag bits");
+    return run_stream(q, stream, "levo_vae_fused_unit_f32");
+}
+
+}  // namespace levo
+
+extern "C" {
+
+LEVO_OPS_API int levo_snakebeta_f32(const float *x, int64_t ldx, const void *alpha_log,
+                                    const void *beta_log, int param_dtype, float *y, int64_t ldy,
+                                    int64_t channels, int64_t time, levo_stream_t stream) {
+    levo::clear_error();
+    if (alpha_log == nullptr || beta_log == nullptr)
+        return levo::set_error(LEVO_OPS_EINVAL, "levo_snakebeta_f32: SnakeBeta parameters are null");
+    if (y == nullptr) return levo::set_error(LEVO_OPS_EINVAL, "levo_snakebeta_f32: output is null");
+    levo::StreamRequest q{};
+    q.u = x;
+    q.ldu = ldx;
+    q.alog = alpha_log;
+    q.blog = beta_log;
+    q.pdtype = param_dtype;
+    q.y_out = y;
+    q.ldy = ldy;
+    q.rows = channels;
+    q.len = time;
+    return levo::run_stream(q, reinterpret_cast<cudaStream_t>(stream), "levo_snakebeta_f32");
+}
+
+LEVO_OPS_API int levo_channel_bias_add_f32(const float *in, const void *bias, int bias_dtype,
+                                           float *out, int64_t channels, int64_t time,
+                                           levo_stream_t stream) {
+    levo::clear_error();
+    if (bias == nullptr)
+        return levo::set_error(LEVO_OPS_EINVAL, "levo_channel_bias_add_f32: bias is null");
+    if (out == nullptr)
+        return levo::set_error(LEVO_OPS_EINVAL, "levo_channel_bias_add_f32: output is null");
+    levo::StreamRequest q{};
+    q.u = in;
+    q.ldu = time;
+    q.bias = bias;
+    q.pdtype = bias_dtype;
+    q.y_out = out;
+    q.ldy = time;
+    q.rows = channels;
+    q.len = time;
+    return levo::run_stream(q, reinterpret_cast<cudaStream_t>(stream), "levo_channel_bias_add_f32");
+}
+
+LEVO_OPS_API int levo_vae_fused_unit_f32(const levo_fused_unit *unit, levo_stream_t stream) {
+    levo::clear_error();
+    if (unit == nullptr)
+        return levo::set_error(LEVO_OPS_EINVAL, "levo_vae_fused_unit_f32: descriptor is null");
+    return levo::fused_unit(*unit, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,690 @@
+// Decoder elementwise chain driver (a4): the stage loop of the Oobleck decoder
+// (reference: src/levo-vae.cpp:172-276) with every elementwise node fused into
+// one HBM pass per convolution output.
+//
+// Per stage (C = stage width, L = stage length), with conv outputs raw (no bias):
+//   upsample conv  -> [UPSAMPLE] x = u + b_up;            y = snake_pre0(x)   12 B/elem
+//   per residual r:
+//     conv.0       -> [POST]     y = snake_post_r(u + b0)                      8 B/elem
+//     conv.1       -> [RESIDUAL] x = x + (u + b1);         y = snake_next(x)  16 B/elem
+//                                 (the last unit skips storing x: 12 B/elem)
+// where snake_next is the next unit's pre activation, the next stage's upsample
+// activation, or the output activation.  The input conv is followed by [ENTRY]
+// y = snake_up0(u + b_in) (8 B/elem).  Every fused unit writes y in place over
+// its conv output, which the next conv then reads.
+//
+// Convolutions are not part of this layer: a callback performs them.  Without
+// one, built-in stand-ins run instead (index-map copies for the input, upsample
+// and output convs; identity aliases for the residual convs).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace levo {
+int fused_unit(const levo_fused_unit &unit, cudaStream_t stream);
+
+namespace {
+
+__global__ void __launch_bounds__(256) conv_standin_kernel(const float *in, int64_t cin, int64_t lin,
+                                                          float *out, int64_t cout, int64_t lout,
+                                                          int32_t stride) {
+    const int64_t n = cout * lout;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t c = e / lout;
+        const int64_t t = e - c * lout;
+        const int64_t sc = c % cin;
+        const int64_t st = t / stride;
+        out[e] = st < lin ? in[sc * lin + st] : 0.f;
+    }
+}
+
+struct SnakeRef {
+    const float *alpha;
+    const float *beta;
+};
+
+struct StageOffsets {
+    int64_t up_alpha, up_beta, up_bias;
+    int64_t pre_alpha[LEVO_VAE_MAX_RESIDUALS], pre_beta[LEVO_VAE_MAX_RESIDUALS];
+    int64_t bias0[LEVO_VAE_MAX_RESIDUALS];
+    int64_t post_alpha[LEVO_VAE_MAX_RESIDUALS], post_beta[LEVO_VAE_MAX_RESIDUALS];
+    int64_t bias1[LEVO_VAE_MAX_RESIDUALS];
+};
+
+struct Layout {
+    int64_t in_bias;
+    StageOffsets stage[LEVO_VAE_MAX_STAGES];
+    int64_t out_alpha, out_beta;
+    int64_t total;
+};
+
+bool valid_topology(const levo_vae_topology &t, std::string *why) {
+    auto bad = [why](const char *m) {
+        *why = m;
+        return false;
+    };
+    if (t.latent_dim <= 0 || t.audio_channels <= 0 || t.entry_width <= 0)
+        return bad("latent_dim, audio_channels and entry_width must be positive");
+    if (t.n_stages < 1 || t.n_stages > LEVO_VAE_MAX_STAGES) return bad("n_stages must be 1..8");
+    if (t.n_residual < 0 || t.n_residual > LEVO_VAE_MAX_RESIDUALS) return bad("n_residual must be 0..4");
+    for (int s = 0; s < t.n_stages; ++s)
+        if (t.stage_width[s] <= 0 || t.stage_stride[s] <= 0) return bad("stage widths and strides must be positive");
+    for (int r = 0; r < t.n_residual; ++r)
+        if (t.dilation[r] <= 0) return bad("dilations must be positive");
+    return true;
+}
+
+Layout make_layout(const levo_vae_topology &t) {
+    Layout l{};
+    int64_t off = 0;
+    l.in_bias = off;
+    off += t.entry_width;
+    int64_t cin = t.entry_width;
+    for (int s = 0; s < t.n_stages; ++s) {
+        const int64_t c = t.stage_width[s];
+        StageOffsets &so = l.stage[s];
+        so.up_alpha = off;
+        off += cin;
+        so.up_beta = off;
+        off += cin;
+        so.up_bias = off;
+        off += c;
+        for (int r = 0; r < t.n_residual; ++r) {
+            so.pre_alpha[r] = off;
+            off += c;
+            so.pre_beta[r] = off;
+            off += c;
+            so.bias0[r] = off;
+            off += c;
+            so.post_alpha[r] = off;
+            off += c;
+            so.post_beta[r] = off;
+            off += c;
+            so.bias1[r] = off;
+            off += c;
+        }
+        cin = c;
+    }
+    l.out_alpha = off;
+    off += cin;
+    l.out_beta = off;
+    off += cin;
+    l.total = off;
+    return l;
+}
+
+int64_t total_upsampling(const levo_vae_topology &t) {
+    int64_t f = 1;
+    for (int s = 0; s < t.n_stages; ++s) f *= t.stage_stride[s];
+    return f;
+}
+
+class DeviceGuard {
+   public:
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&previous_) != cudaSuccess) previous_ = -1;
+        if (previous_ != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        if (previous_ >= 0) cudaSetDevice(previous_);
+    }
+
+   private:
+    int previous_ = -1;
+};
+
+struct TimedLaunch {
+    int kclass;
+    int ev_start, ev_end;
+    double bytes, elems;
+};
+
+}  // namespace
+}  // namespace levo
+
+struct levo_vae_chain {
+    int device = 0;
+    levo_vae_topology topo{};
+    levo::Layout layout{};
+    int64_t max_frames = 0;
+    int64_t max_elems = 0;
+    float *params = nullptr;
+    float *X = nullptr;
+    float *A = nullptr;
+    float *B = nullptr;
+    float *lat[2] = {nullptr, nullptr};
+    float *audio[2] = {nullptr, nullptr};
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t computed[2] = {nullptr, nullptr};
+    cudaEvent_t copied[2] = {nullptr, nullptr};
+    levo_conv_fn conv = nullptr;
+    void *conv_user = nullptr;
+    // timing
+    std::vector<cudaEvent_t> events;
+    int next_event = 0;
+    std::vector<levo::TimedLaunch> launches;
+    levo_kernel_timing totals[LEVO_KCLASS_COUNT] = {};
+};
+
+namespace levo {
+namespace {
+
+int cuda_fail(cudaError_t err, const std::string &what) {
+    return set_error(err == cudaErrorMemoryAllocation ? LEVO_OPS_ENOMEM : LEVO_OPS_ECUDA,
+                     what + ": " + cudaGetErrorString(err));
+}
+
+void free_chain(levo_vae_chain *c) {
+    if (c == nullptr) return;
+    DeviceGuard guard(c->device);
+    cudaFree(c->params);
+    cudaFree(c->X);
+    cudaFree(c->A);
+    cudaFree(c->B);
+    for (int i = 0; i < 2; ++i) {
+        cudaFree(c->lat[i]);
+        cudaFree(c->audio[i]);
+        if (c->computed[i]) cudaEventDestroy(c->computed[i]);
+        if (c->copied[i]) cudaEventDestroy(c->copied[i]);
+    }
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    for (cudaEvent_t e : c->events) cudaEventDestroy(e);
+    delete c;
+}
+
+int take_event(levo_vae_chain *c, int *index) {
+    if (c->next_event >= static_cast<int>(c->events.size())) {
+        cudaEvent_t e = nullptr;
+        const cudaError_t err = cudaEventCreate(&e);
+        if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain timing event");
+        c->events.push_back(e);
+    }
+    *index = c->next_event++;
+    return LEVO_OPS_OK;
+}
+
+// Runs `body` and, when timing, brackets it with a pair of events.
+template <class F>
+int timed(levo_vae_chain *c, bool timing, int kclass, double bytes, double elems, cudaStream_t s,
+          F &&body) {
+    int e0 = -1, e1 = -1;
+    if (timing) {
+        int rc = take_event(c, &e0);
+        if (rc == LEVO_OPS_OK) rc = take_event(c, &e1);
+        if (rc != LEVO_OPS_OK) return rc;
+        cudaEventRecord(c->events[e0], s);
+    }
+    const int rc = body();
+    if (rc != LEVO_OPS_OK) return rc;
+    if (timing) {
+        cudaEventRecord(c->events[e1], s);
+        c->launches.push_back(TimedLaunch{kclass, e0, e1, bytes, elems});
+    }
+    return LEVO_OPS_OK;
+}
+
+int run_unit(levo_vae_chain *c, bool timing, int kclass, const levo_fused_unit &u, cudaStream_t s) {
+    const double n = static_cast<double>(u.channels) * static_cast<double>(u.time);
+    const double bytes =
+        4.0 * n * (1 + (u.residual ? 1 : 0) + (u.x_out ? 1 : 0) + (u.y_out ? 1 : 0));
+    return timed(c, timing, kclass, bytes, n, s, [&] { return fused_unit(u, s); });
+}
+
+int run_conv(levo_vae_chain *c, bool timing, levo_conv_call &call, cudaStream_t s) {
+    call.result = call.output;
+    if (c->conv) {
+        const int rc = timed(c, timing, LEVO_KCLASS_CONV, 0.0, 0.0, s, [&] {
+            const int r = c->conv(c->conv_user, &call, reinterpret_cast<levo_stream_t>(s));
+            if (r != 0)
+                return set_error(LEVO_OPS_ECUDA, "levo_vae_chain: convolution callback failed (kind " +
+                                                     std::to_string(call.kind) + ", code " +
+                                                     std::to_string(r) + ")");
+            return static_cast<int>(LEVO_OPS_OK);
+        });
+        if (rc != LEVO_OPS_OK) return rc;
+        if (call.result != call.output &&
+            (call.result != call.input || call.in_channels != call.out_channels ||
+             call.in_length != call.out_length))
+            return set_error(LEVO_OPS_EINVAL,
+                             "levo_vae_chain: a convolution callback may only alias an "
+                             "identically shaped input");
+        return LEVO_OPS_OK;
+    }
+    if (call.kind == LEVO_CONV_RES0 || call.kind == LEVO_CONV_RES1) {
+        call.result = const_cast<float *>(call.input);
+        return LEVO_OPS_OK;
+    }
+    const double n_out = static_cast<double>(call.out_channels) * call.out_length;
+    const double n_in = static_cast<double>(call.in_channels) * call.in_length;
+    return timed(c, timing, LEVO_KCLASS_CONV, 4.0 * (n_in + n_out), n_out, s, [&] {
+        return levo_conv_standin_f32(call.input, call.in_channels, call.in_length, call.output,
+                                     call.out_channels, call.out_length,
+                                     call.kind == LEVO_CONV_UPSAMPLE ? call.stride : 1,
+                                     reinterpret_cast<levo_stream_t>(s));
+    });
+}
+
+float *other_of(levo_vae_chain *c, const float *cur) { return cur == c->A ? c->B : c->A; }
+
+int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *audio_out,
+               uint32_t flags, cudaStream_t s) {
+    const levo_vae_topology &t = c->topo;
+    const Layout &l = c->layout;
+    const float *P = c->params;
+    const bool timing = (flags & LEVO_CHAIN_TIMING) != 0;
+    auto snake_of = [&](int stage, int unit) -> SnakeRef {
+        // Activation applied before conv `unit` of `stage`; unit == n_residual
+        // means the next stage's upsample activation (or the output one).
+        if (stage < t.n_stages && unit < t.n_residual)
+            return {P + l.stage[stage].pre_alpha[unit], P + l.stage[stage].pre_beta[unit]};
+        if (stage + 1 < t.n_stages) return {P + l.stage[stage + 1].up_alpha, P + l.stage[stage + 1].up_beta};
+        return {P + l.out_alpha, P + l.out_beta};
+    };
+
+    // Input conv + ENTRY unit.
+    levo_conv_call call{};
+    call.kind = LEVO_CONV_INPUT;
+    call.stage = -1;
+    call.unit = -1;
+    call.kernel = 7;
+    call.stride = 1;
+    call.padding = 3;
+    call.dilation = 1;
+    call.input = latent;
+    call.in_channels = t.latent_dim;
+    call.in_length = frames;
+    call.output = c->B;
+    call.out_channels = t.entry_width;
+    call.out_length = frames;
+    int rc = run_conv(c, timing, call, s);
+    if (rc != LEVO_OPS_OK) return rc;
+    float *cur = call.result;
+    {
+        levo_fused_unit u{};
+        u.u = cur;
+        u.bias = P + l.in_bias;
+        u.alpha_log = P + l.stage[0].up_alpha;
+        u.beta_log = P + l.stage[0].up_beta;
+        u.y_out = cur;
+        u.channels = t.entry_width;
+        u.time = frames;
+        u.param_dtype = LEVO_DTYPE_F32;
+        rc = run_unit(c, timing, LEVO_KCLASS_ENTRY, u, s);
+        if (rc != LEVO_OPS_OK) return rc;
+    }
+
+    int64_t cin = t.entry_width;
+    int64_t len = frames;
+    for (int st = 0; st < t.n_stages; ++st) {
+        const int64_t cout = t.stage_width[st];
+        const int64_t lout = len * t.stage_stride[st];
+        const StageOffsets &so = l.stage[st];
+        call = levo_conv_call{};
+        call.kind = LEVO_CONV_UPSAMPLE;
+        call.stage = st;
+        call.unit = -1;
+        call.kernel = 2 * t.stage_stride[st];
+        call.stride = t.stage_stride[st];
+        call.padding = (t.stage_stride[st] + 1) / 2;
+        call.dilation = 1;
+        call.input = cur;
+        call.in_channels = cin;
+        call.in_length = len;
+        call.output = other_of(c, cur);
+        call.out_channels = cout;
+        call.out_length = lout;
+        rc = run_conv(c, timing, call, s);
+        if (rc != LEVO_OPS_OK) return rc;
+        cur = call.result;
+        {
+            const SnakeRef sn = snake_of(st, 0);
+            levo_fused_unit u{};
+            u.u = cur;
+            u.bias = P + so.up_bias;
+            u.alpha_log = sn.alpha;
+            u.beta_log = sn.beta;
+            u.x_out = t.n_residual > 0 ? c->X : nullptr;
+            u.y_out = cur;
+            u.channels = cout;
+            u.time = lout;
+            u.param_dtype = LEVO_DTYPE_F32;
+            rc = run_unit(c, timing, LEVO_KCLASS_UPSAMPLE, u, s);
+            if (rc != LEVO_OPS_OK) return rc;
+        }
+        for (int r = 0; r < t.n_residual; ++r) {
+            call = levo_conv_call{};
+            call.kind = LEVO_CONV_RES0;
+            call.stage = st;
+            call.unit = r;
+            call.kernel = 7;
+            call.stride = 1;
+            call.padding = 3 * t.dilation[r];
+            call.dilation = t.dilation[r];
+            call.input = cur;
+            call.in_channels = cout;
+            call.in_length = lout;
+            call.output = other_of(c, cur);
+            call.out_channels = cout;
+            call.out_length = lout;
+            rc = run_conv(c, timing, call, s);
+            if (rc != LEVO_OPS_OK) return rc;
+            cur = call.result;
+            {
+                levo_fused_unit u{};
+                u.u = cur;
+                u.bias = P + so.bias0[r];
+                u.alpha_log = P + so.post_alpha[r];
+                u.beta_log = P + so.post_beta[r];
+                u.y_out = cur;
+                u.channels = cout;
+                u.time = lout;
+                u.param_dtype = LEVO_DTYPE_F32;
+                rc = run_unit(c, timing, LEVO_KCLASS_POST, u, s);
+                if (rc != LEVO_OPS_OK) return rc;
+            }
+            call = levo_conv_call{};
+            call.kind = LEVO_CONV_RES1;
+            call.stage = st;
+            call.unit = r;
+            call.kernel = 1;
+            call.stride = 1;
+            call.padding = 0;
+            call.dilation = 1;
+            call.input = cur;
+            call.in_channels = cout;
+            call.in_length = lout;
+            call.output = other_of(c, cur);
+            call.out_channels = cout;
+            call.out_length = lout;
+            rc = run_conv(c, timing, call, s);
+            if (rc != LEVO_OPS_OK) return rc;
+            cur = call.result;
+            {
+                const SnakeRef sn = snake_of(st, r + 1);
+                levo_fused_unit u{};
+                u.u = cur;
+                u.bias = P + so.bias1[r];
+                u.residual = c->X;
+                u.alpha_log = sn.alpha;
+                u.beta_log = sn.beta;
+                u.x_out = r + 1 < t.n_residual ? c->X : nullptr;
+                u.y_out = cur;
+                u.channels = cout;
+                u.time = lout;
+                u.param_dtype = LEVO_DTYPE_F32;
+                rc = run_unit(c, timing, LEVO_KCLASS_RESIDUAL, u, s);
+                if (rc != LEVO_OPS_OK) return rc;
+            }
+        }
+        cin = cout;
+        len = lout;
+    }
+
+    // Output conv (no bias) + optional tanh epilogue.
+    call = levo_conv_call{};
+    call.kind = LEVO_CONV_OUTPUT;
+    call.stage = -1;
+    call.unit = -1;
+    call.kernel = 7;
+    call.stride = 1;
+    call.padding = 3;
+    call.dilation = 1;
+    call.input = cur;
+    call.in_channels = cin;
+    call.in_length = len;
+    call.output = audio_out;
+    call.out_channels = t.audio_channels;
+    call.out_length = len;
+    rc = run_conv(c, timing, call, s);
+    if (rc != LEVO_OPS_OK) return rc;
+    if (call.result != audio_out)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain: the output convolution must write the audio buffer");
+    if (flags & LEVO_CHAIN_TANH) {
+        levo_fused_unit u{};
+        u.u = audio_out;
+        u.y_out = audio_out;
+        u.channels = t.audio_channels;
+        u.time = len;
+        u.param_dtype = LEVO_DTYPE_F32;
+        u.flags = LEVO_FUSED_TANH;
+        rc = run_unit(c, timing, LEVO_KCLASS_EPILOGUE, u, s);
+        if (rc != LEVO_OPS_OK) return rc;
+    }
+    return LEVO_OPS_OK;
+}
+
+int check_decode_args(levo_vae_chain *c, int64_t frames, uint32_t flags, const char *what) {
+    if (c == nullptr) return set_error(LEVO_OPS_EINVAL, std::string(what) + ": chain is null");
+    if (frames <= 0 || frames > c->max_frames)
+        return set_error(LEVO_OPS_EINVAL,
+                         std::string(what) + ": latent frame count must be in 1..max_frames");
+    if (flags & ~(LEVO_CHAIN_TANH | LEVO_CHAIN_TIMING))
+        return set_error(LEVO_OPS_EINVAL, std::string(what) + ": unknown flag bits");
+    return LEVO_OPS_OK;
+}
+
+}  // namespace
+}  // namespace levo
+
+extern "C" {
+
+LEVO_OPS_API int levo_vae_topology_reference(levo_vae_topology *out) {
+    levo::clear_error();
+    if (out == nullptr) return levo::set_error(LEVO_OPS_EINVAL, "levo_vae_topology_reference: out is null");
+    levo_vae_topology t{};
+    t.latent_dim = 64;
+    t.audio_channels = 2;
+    t.entry_width = 2048;
+    t.n_stages = 5;
+    const int32_t widths[5] = {1024, 512, 256, 128, 128};
+    const int32_t strides[5] = {10, 6, 4, 4, 2};
+    for (int s = 0; s < 5; ++s) {
+        t.stage_width[s] = widths[s];
+        t.stage_stride[s] = strides[s];
+    }
+    t.n_residual = 3;
+    t.dilation[0] = 1;
+    t.dilation[1] = 3;
+    t.dilation[2] = 9;
+    *out = t;
+    return LEVO_OPS_OK;
+}
+
+LEVO_OPS_API int64_t levo_vae_param_count(const levo_vae_topology *topology) {
+    levo::clear_error();
+    std::string why;
+    if (topology == nullptr || !levo::valid_topology(*topology, &why))
+        return levo::set_error(LEVO_OPS_EINVAL, "levo_vae_param_count: invalid topology: " + why);
+    return levo::make_layout(*topology).total;
+}
+
+LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int64_t in_length,
+                                       float *out, int64_t out_channels, int64_t out_length,
+                                       int32_t stride, levo_stream_t stream) {
+    using namespace levo;
+    if (in == nullptr || out == nullptr)
+        return set_error(LEVO_OPS_EINVAL, "levo_conv_standin_f32: required pointer is null");
+    if (in_channels <= 0 || in_length <= 0 || out_channels < 0 || out_length < 0 || stride <= 0)
+        return set_error(LEVO_OPS_EINVAL, "levo_conv_standin_f32: invalid shape or stride");
+    const int64_t n = out_channels * out_length;
+    if (n == 0) return LEVO_OPS_OK;
+    const int64_t grid = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
+    conv_standin_kernel<<<static_cast<unsigned>(grid), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        in, in_channels, in_length, out, out_channels, out_length, stride);
+    return check_launch("levo_conv_standin_f32");
+}
+
+LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topology *topology,
+                                       const float *params_host, int64_t max_frames,
+                                       levo_conv_fn conv, void *conv_user, int device) {
+    using namespace levo;
+    clear_error();
+    if (out == nullptr || topology == nullptr || params_host == nullptr)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_create: required pointer is null");
+    *out = nullptr;
+    std::string why;
+    if (!valid_topology(*topology, &why))
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_create: invalid topology: " + why);
+    if (max_frames <= 0) return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_create: max_frames must be positive");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_create: no such CUDA device");
+
+    levo_vae_chain *c = new (std::nothrow) levo_vae_chain();
+    if (c == nullptr) return set_error(LEVO_OPS_ENOMEM, "levo_vae_chain_create: out of host memory");
+    c->device = device;
+    c->topo = *topology;
+    c->layout = make_layout(*topology);
+    c->max_frames = max_frames;
+    c->conv = conv;
+    c->conv_user = conv_user;
+    const levo_vae_topology &t = c->topo;
+    int64_t elems = static_cast<int64_t>(t.entry_width) * max_frames;
+    int64_t len = max_frames;
+    int64_t cin = t.entry_width;
+    for (int s = 0; s < t.n_stages; ++s) {
+        if (len > (int64_t(1) << 40) / t.stage_stride[s]) {
+            free_chain(c);
+            return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_create: decoded length overflows");
+        }
+        elems = std::max(elems, cin * len);
+        len *= t.stage_stride[s];
+        elems = std::max(elems, static_cast<int64_t>(t.stage_width[s]) * len);
+        cin = t.stage_width[s];
+    }
+    c->max_elems = elems;
+    const size_t act_bytes = static_cast<size_t>(elems) * sizeof(float);
+    const size_t lat_bytes = static_cast<size_t>(t.latent_dim) * max_frames * sizeof(float);
+    const size_t audio_bytes = static_cast<size_t>(t.audio_channels) * len * sizeof(float);
+
+    DeviceGuard guard(device);
+    cudaError_t err = cudaSuccess;
+    const size_t param_bytes = static_cast<size_t>(c->layout.total) * sizeof(float);
+    if (err == cudaSuccess) err = cudaMalloc(&c->params, param_bytes);
+    if (err == cudaSuccess) err = cudaMalloc(&c->X, act_bytes);
+    if (err == cudaSuccess) err = cudaMalloc(&c->A, act_bytes);
+    if (err == cudaSuccess) err = cudaMalloc(&c->B, act_bytes);
+    for (int i = 0; i < 2 && err == cudaSuccess; ++i) {
+        err = cudaMalloc(&c->lat[i], lat_bytes);
+        if (err == cudaSuccess) err = cudaMalloc(&c->audio[i], audio_bytes);
+        if (err == cudaSuccess) err = cudaEventCreateWithFlags(&c->computed[i], cudaEventDisableTiming);
+        if (err == cudaSuccess) err = cudaEventCreateWithFlags(&c->copied[i], cudaEventDisableTiming);
+    }
+    if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaMemcpy(c->params, params_host, param_bytes, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        const int rc = cuda_fail(err, "levo_vae_chain_create");
+        free_chain(c);
+        return rc;
+    }
+    *out = c;
+    return LEVO_OPS_OK;
+}
+
+LEVO_OPS_API void levo_vae_chain_destroy(levo_vae_chain *chain) {
+    if (chain == nullptr) return;
+    {
+        levo::DeviceGuard guard(chain->device);
+        cudaDeviceSynchronize();
+    }
+    levo::free_chain(chain);
+}
+
+LEVO_OPS_API int levo_vae_chain_decode(levo_vae_chain *chain, const float *latent, int64_t frames,
+                                       float *audio, uint32_t flags, levo_stream_t stream) {
+    using namespace levo;
+    clear_error();
+    int rc = check_decode_args(chain, frames, flags, "levo_vae_chain_decode");
+    if (rc != LEVO_OPS_OK) return rc;
+    if (latent == nullptr || audio == nullptr)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_decode: required pointer is null");
+    if (!aligned_to(latent, 4) || !aligned_to(audio, 4))
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_decode: pointer is not 4-byte aligned");
+    DeviceGuard guard(chain->device);
+    return decode_one(chain, latent, frames, audio, flags, reinterpret_cast<cudaStream_t>(stream));
+}
+
+LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const float *latents_host,
+                                               int64_t windows, int64_t frames, float *audio_host,
+                                               uint32_t flags, levo_cancel_fn cancel,
+                                               void *cancel_user, levo_stream_t stream) {
+    using namespace levo;
+    clear_error();
+    int rc = check_decode_args(chain, frames, flags, "levo_vae_chain_decode_windows");
+    if (rc != LEVO_OPS_OK) return rc;
+    if (latents_host == nullptr || audio_host == nullptr || windows < 0)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_decode_windows: invalid host buffers or window count");
+    DeviceGuard guard(chain->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const levo_vae_topology &t = chain->topo;
+    const int64_t lat_elems = static_cast<int64_t>(t.latent_dim) * frames;
+    const int64_t audio_elems = static_cast<int64_t>(t.audio_channels) * frames * total_upsampling(t);
+    bool pending[2] = {false, false};
+    cudaError_t err = cudaSuccess;
+    for (int64_t w = 0; w < windows; ++w) {
+        if (cancel != nullptr && cancel(cancel_user) != 0) {
+            cudaStreamSynchronize(s);
+            cudaStreamSynchronize(chain->copy_stream);
+            return set_error(LEVO_OPS_ECANCELLED,
+                             "levo_vae_chain_decode_windows: cancelled before window " + std::to_string(w));
+        }
+        const int slot = static_cast<int>(w & 1);
+        // The slot's previous audio must have left the device before reuse.
+        if (pending[slot]) err = cudaStreamWaitEvent(s, chain->copied[slot], 0);
+        if (err == cudaSuccess)
+            err = cudaMemcpyAsync(chain->lat[slot], latents_host + w * lat_elems,
+                                  static_cast<size_t>(lat_elems) * sizeof(float), cudaMemcpyHostToDevice, s);
+        if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: latent upload");
+        rc = decode_one(chain, chain->lat[slot], frames, chain->audio[slot], flags, s);
+        if (rc != LEVO_OPS_OK) {
+            cudaStreamSynchronize(s);
+            cudaStreamSynchronize(chain->copy_stream);
+            return rc;
+        }
+        err = cudaEventRecord(chain->computed[slot], s);
+        if (err == cudaSuccess) err = cudaStreamWaitEvent(chain->copy_stream, chain->computed[slot], 0);
+        if (err == cudaSuccess)
+            err = cudaMemcpyAsync(audio_host + w * audio_elems, chain->audio[slot],
+                                  static_cast<size_t>(audio_elems) * sizeof(float), cudaMemcpyDeviceToHost,
+                                  chain->copy_stream);
+        if (err == cudaSuccess) err = cudaEventRecord(chain->copied[slot], chain->copy_stream);
+        if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: audio download");
+        pending[slot] = true;
+    }
+    err = cudaStreamSynchronize(chain->copy_stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: synchronize");
+    return LEVO_OPS_OK;
+}
+
+LEVO_OPS_API int levo_vae_chain_timing(levo_vae_chain *chain, levo_kernel_timing *out, int reset) {
+    using namespace levo;
+    clear_error();
+    if (chain == nullptr || out == nullptr)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_timing: required pointer is null");
+    DeviceGuard guard(chain->device);
+    for (const TimedLaunch &tl : chain->launches) {
+        const cudaError_t err = cudaEventSynchronize(chain->events[tl.ev_end]);
+        if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_timing");
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, chain->events[tl.ev_start], chain->events[tl.ev_end]);
+        levo_kernel_timing &k = chain->totals[tl.kclass];
+        k.launches += 1;
+        k.milliseconds += ms;
+        k.algorithmic_bytes += tl.bytes;
+        k.elements += tl.elems;
+    }
+    chain->launches.clear();
+    chain->next_event = 0;
+    std::memcpy(out, chain->totals, sizeof(chain->totals));
+    if (reset) std::memset(chain->totals, 0, sizeof(chain->totals));
+    return LEVO_OPS_OK;
+}
+
+}  // extern "C"

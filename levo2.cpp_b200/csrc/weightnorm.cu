@@ -1,0 +1,159 @@
+// Weight-norm fold (a9): w[o][:] = v[o][:] * (g[o] / ||v[o][:]||).
+//
+// One CTA per row.  Rows up to 16384 values stay in registers (one HBM read of
+// v, one write of w: 8 B per element); longer rows are streamed twice (the
+// second read mostly hits L2).  The arithmetic follows the reference's numpy
+// expression (convert/convert_vae.py:196-199): norm = sqrt(sum(v*v)) in F32,
+// scale = g / norm, w = v * scale.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace levo {
+namespace {
+
+struct WnArgs {
+    const float *v;
+    const float *g;
+    float *w;
+    float *norms;
+    int64_t rows;
+    int64_t cols;
+};
+
+__device__ __forceinline__ float block_sum(float s, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __syncthreads();  // red is reused across rows
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float t = 0.f;
+    const int warps = blockDim.x >> 5;
+    for (int w = 0; w < warps; ++w) t += red[w];
+    return t;
+}
+
+__device__ __forceinline__ float row_scale(const WnArgs &a, int64_t row, float sumsq) {
+    const float norm = __fsqrt_rn(sumsq);
+    if (a.norms && threadIdx.x == 0) a.norms[row] = norm;
+    return __fdiv_rn(a.g[row], norm);
+}
+
+// VPT > 0: the row is register resident (VPT 8-float vectors per thread).
+// VPT == 0: the row is streamed twice.
+template <int VPT>
+__global__ void __launch_bounds__(256) weightnorm_vec_kernel(const WnArgs a) {
+    __shared__ float red[32];
+    const int64_t nvec = a.cols / 8;
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        const float *vr = a.v + row * a.cols;
+        float *wr = a.w + row * a.cols;
+        if constexpr (VPT > 0) {
+            f32x8 buf[VPT];
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int64_t vi = k * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+                if (vi < nvec) buf[k] = ld8(vr + vi * 8);
+            }
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int64_t vi = k * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+                if (vi < nvec) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) s = fmaf(buf[k].v[j], buf[k].v[j], s);
+                }
+            }
+            const float scale = row_scale(a, row, block_sum(s, red));
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int64_t vi = k * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+                if (vi < nvec) {
+                    f32x8 o;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) o.v[j] = __fmul_rn(buf[k].v[j], scale);
+                    st8(wr + vi * 8, o);
+                }
+            }
+        } else {
+            float s = 0.f;
+            for (int64_t vi = threadIdx.x; vi < nvec; vi += blockDim.x) {
+                const f32x8 b = ld8(vr + vi * 8);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s = fmaf(b.v[j], b.v[j], s);
+            }
+            const float scale = row_scale(a, row, block_sum(s, red));
+            for (int64_t vi = threadIdx.x; vi < nvec; vi += blockDim.x) {
+                f32x8 b = ld8(vr + vi * 8);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) b.v[j] = __fmul_rn(b.v[j], scale);
+                st8(wr + vi * 8, b);
+            }
+        }
+    }
+}
+
+// Any row length / alignment.
+__global__ void __launch_bounds__(256) weightnorm_scalar_kernel(const WnArgs a) {
+    __shared__ float red[32];
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        const float *vr = a.v + row * a.cols;
+        float *wr = a.w + row * a.cols;
+        float s = 0.f;
+        for (int64_t j = threadIdx.x; j < a.cols; j += blockDim.x) s = fmaf(vr[j], vr[j], s);
+        const float scale = row_scale(a, row, block_sum(s, red));
+        for (int64_t j = threadIdx.x; j < a.cols; j += blockDim.x) wr[j] = __fmul_rn(vr[j], scale);
+    }
+}
+
+template <int VPT>
+void launch_wn(const WnArgs &a, int threads, cudaStream_t stream) {
+    const int64_t grid = std::min<int64_t>(a.rows, static_cast<int64_t>(sm_count()) * 64);
+    weightnorm_vec_kernel<VPT><<<static_cast<unsigned>(grid), threads, 0, stream>>>(a);
+}
+
+}  // namespace
+}  // namespace levo
+
+extern "C" {
+
+LEVO_OPS_API int levo_weightnorm_f32(const float *v, const float *g, float *w, float *norms_out,
+                                     int64_t rows, int64_t cols, levo_stream_t stream) {
+    using namespace levo;
+    clear_error();
+    if (v == nullptr || g == nullptr || w == nullptr)
+        return set_error(LEVO_OPS_EINVAL, "levo_weightnorm_f32: required pointer is null");
+    if (rows < 0 || cols < 0) return set_error(LEVO_OPS_EINVAL, "levo_weightnorm_f32: negative shape");
+    const void *ptrs[4] = {v, g, w, norms_out};
+    for (const void *p : ptrs)
+        if (p && !aligned_to(p, 4))
+            return set_error(LEVO_OPS_EINVAL, "levo_weightnorm_f32: pointer is not 4-byte aligned");
+    if (rows == 0 || cols == 0) return LEVO_OPS_OK;
+    const WnArgs a{v, g, w, norms_out, rows, cols};
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const bool vec = cols % 8 == 0 && aligned_to(v, 32) && aligned_to(w, 32);
+    if (!vec) {
+        const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * 64);
+        weightnorm_scalar_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(a);
+        return check_launch("levo_weightnorm_f32");
+    }
+    const int64_t nvec = cols / 8;
+    // 128 threads while the row fits in 8 vectors per thread (single-wave
+    // grids for ~1000-row weights), then 256 threads, then the streamed form.
+    const int threads = nvec <= 128 * 8 ? 128 : 256;
+    const int64_t vpt = (nvec + threads - 1) / threads;
+    switch (vpt) {
+        case 1: launch_wn<1>(a, threads, s); break;
+        case 2: launch_wn<2>(a, threads, s); break;
+        case 3: launch_wn<3>(a, threads, s); break;
+        case 4: launch_wn<4>(a, threads, s); break;
+        case 5: launch_wn<5>(a, threads, s); break;
+        case 6: launch_wn<6>(a, threads, s); break;
+        case 7: launch_wn<7>(a, threads, s); break;
+        case 8: launch_wn<8>(a, threads, s); break;
+        default: launch_wn<0>(a, 256, s); break;
+    }
+    return check_launch("levo_weightnorm_f32");
+}
+
+}  // extern "C"

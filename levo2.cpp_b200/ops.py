@@ -1,0 +1,404 @@
+"""ctypes binding of liblevo_b200.so (the C ABI of include/levo_ops.h).
+
+The library is loaded from this package directory; there is no fallback: when
+it is missing every call raises, so nothing silently runs on the CPU.  The
+`*_t` helpers take torch CUDA tensors (torch is only the device-memory and
+stream plumbing here) and pass raw pointers plus the current stream.
+
+Error behaviour mirrors the reference: invalid arguments raise ValueError
+(the reference throws std::invalid_argument, src/levo-audio-ops.cpp:45-47),
+everything else raises LevoOpsError with the library's thread-local message.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+from typing import Optional
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblevo_b200.so"
+
+OK, EINVAL, ELAUNCH, EUNSUPPORTED, ENONFINITE, ECANCELLED, ENOMEM, ECUDA = 0, -1, -2, -3, -4, -5, -6, -7
+DTYPE_F32, DTYPE_F16 = 0, 1
+FUSED_TANH = 1
+NORM_F16_BOUNDARY = 1
+CHAIN_TANH, CHAIN_TIMING = 1, 2
+KCLASS_NAMES = ("entry", "upsample", "post", "residual", "epilogue", "conv")
+CONV_INPUT, CONV_UPSAMPLE, CONV_RES0, CONV_RES1, CONV_OUTPUT = range(5)
+MAX_STAGES, MAX_RESIDUALS = 8, 4
+
+
+class LevoOpsError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[levo_ops {code}] {message}")
+        self.code = code
+
+
+class LevoCancelled(LevoOpsError):
+    pass
+
+
+class Topology(ctypes.Structure):
+    _fields_ = [
+        ("latent_dim", ctypes.c_int32),
+        ("audio_channels", ctypes.c_int32),
+        ("entry_width", ctypes.c_int32),
+        ("n_stages", ctypes.c_int32),
+        ("stage_width", ctypes.c_int32 * MAX_STAGES),
+        ("stage_stride", ctypes.c_int32 * MAX_STAGES),
+        ("n_residual", ctypes.c_int32),
+        ("dilation", ctypes.c_int32 * MAX_RESIDUALS),
+    ]
+
+    def as_list(self) -> list[int]:
+        """Flat integer form: latent_dim, audio_channels, entry_width, S, widths[S], strides[S], R."""
+        s = self.n_stages
+        return ([self.latent_dim, self.audio_channels, self.entry_width, s]
+                + list(self.stage_width[:s]) + list(self.stage_stride[:s]) + [self.n_residual])
+
+    def upsampling(self) -> int:
+        f = 1
+        for i in range(self.n_stages):
+            f *= self.stage_stride[i]
+        return f
+
+
+class FusedUnit(ctypes.Structure):
+    _fields_ = [
+        ("u", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("alpha_log", ctypes.c_void_p),
+        ("beta_log", ctypes.c_void_p),
+        ("x_out", ctypes.c_void_p),
+        ("y_out", ctypes.c_void_p),
+        ("channels", ctypes.c_int64),
+        ("time", ctypes.c_int64),
+        ("param_dtype", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+    ]
+
+
+class ConvCall(ctypes.Structure):
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("stage", ctypes.c_int32),
+        ("unit", ctypes.c_int32),
+        ("kernel", ctypes.c_int32),
+        ("stride", ctypes.c_int32),
+        ("padding", ctypes.c_int32),
+        ("dilation", ctypes.c_int32),
+        ("input", ctypes.c_void_p),
+        ("in_channels", ctypes.c_int64),
+        ("in_length", ctypes.c_int64),
+        ("output", ctypes.c_void_p),
+        ("out_channels", ctypes.c_int64),
+        ("out_length", ctypes.c_int64),
+        ("result", ctypes.c_void_p),
+    ]
+
+
+class KernelTiming(ctypes.Structure):
+    _fields_ = [
+        ("launches", ctypes.c_int64),
+        ("milliseconds", ctypes.c_double),
+        ("algorithmic_bytes", ctypes.c_double),
+        ("elements", ctypes.c_double),
+    ]
+
+
+CONV_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ConvCall), ctypes.c_void_p)
+CANCEL_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_U32 = ctypes.c_uint32
+_F = ctypes.c_float
+_INT = ctypes.c_int
+
+# name -> (restype, argtypes); every symbol include/levo_ops.h declares.
+SIGNATURES = {
+    "levo_ops_abi_version": (_U32, []),
+    "levo_ops_last_error": (ctypes.c_char_p, []),
+    "levo_snakebeta_f32": (_INT, [_P, _I64, _P, _P, _INT, _P, _I64, _I64, _I64, _P]),
+    "levo_channel_bias_add_f32": (_INT, [_P, _P, _INT, _P, _I64, _I64, _P]),
+    "levo_vae_fused_unit_f32": (_INT, [ctypes.POINTER(FusedUnit), _P]),
+    "levo_vae_topology_reference": (_INT, [ctypes.POINTER(Topology)]),
+    "levo_vae_param_count": (_I64, [ctypes.POINTER(Topology)]),
+    "levo_vae_chain_create": (_INT, [ctypes.POINTER(_P), ctypes.POINTER(Topology), _P, _I64, CONV_FN, _P, _INT]),
+    "levo_vae_chain_destroy": (None, [_P]),
+    "levo_vae_chain_decode": (_INT, [_P, _P, _I64, _P, _U32, _P]),
+    "levo_vae_chain_decode_windows": (_INT, [_P, _P, _I64, _I64, _P, _U32, CANCEL_FN, _P, _P]),
+    "levo_vae_chain_timing": (_INT, [_P, ctypes.POINTER(KernelTiming), _INT]),
+    "levo_conv_standin_f32": (_INT, [_P, _I64, _I64, _P, _I64, _I64, _I32, _P]),
+    "levo_add_rmsnorm_f16": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _F, _U32, _P]),
+    "levo_add_rmsnorm_f32": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _F, _U32, _P]),
+    "levo_add_layernorm_f16": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _U32, _P]),
+    "levo_add_layernorm_f32": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _U32, _P]),
+    "levo_weightnorm_f32": (_INT, [_P, _P, _P, _P, _I64, _I64, _P]),
+    "levo_cfg_combine_f32": (_INT, [_P, _P, _P, _I64, _F, _P]),
+    "levo_flow_incontext_f32": (_INT, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
+    "levo_euler_cfg_step_f32": (_INT, [_P, _P, _P, _I64, _I32, _F, _I64, _P, _P]),
+    "levo_cfg_euler_multi_f32": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _F, _F, _P, _P]),
+}
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads liblevo_b200.so (raises when it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise LevoOpsError(ECUDA, f"{LIB_PATH} is missing; build it with __graft_entry__.build()")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().levo_ops_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(code: int) -> None:
+    if code == OK:
+        return
+    msg = last_error()
+    if code == EINVAL:
+        raise ValueError(msg)
+    if code == ECANCELLED:
+        raise LevoCancelled(code, msg)
+    raise LevoOpsError(code, msg)
+
+
+# ---------------------------------------------------------------------------
+# torch convenience layer (device memory + current stream)
+# ---------------------------------------------------------------------------
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device=None) -> int:
+    import torch
+
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("levo_b200 ops take CUDA tensors")
+
+
+def _pdtype(t) -> int:
+    import torch
+
+    if t.dtype == torch.float32:
+        return DTYPE_F32
+    if t.dtype == torch.float16:
+        return DTYPE_F16
+    raise ValueError("parameters must be float32 or float16")
+
+
+def snakebeta_t(x, alpha_log, beta_log, out=None):
+    """y = x + sin(x*exp(alpha_log))^2 / (exp(beta_log)+1e-9) over [C, T] (row stride honoured)."""
+    import torch
+
+    _require_cuda(x, alpha_log, beta_log)
+    if x.dim() != 2 or x.dtype != torch.float32 or x.stride(1) != 1:
+        raise ValueError("SnakeBeta input must be F32 [channels, time] with unit time stride")
+    if alpha_log.dtype != beta_log.dtype:
+        raise ValueError("alpha_log and beta_log must share a dtype")
+    if alpha_log.numel() != x.shape[0] or beta_log.numel() != x.shape[0]:
+        raise ValueError("SnakeBeta parameters must have shape [1, channels, 1]")
+    y = torch.empty_like(x, memory_format=torch.contiguous_format) if out is None else out
+    check(lib().levo_snakebeta_f32(_ptr(x), x.stride(0), _ptr(alpha_log), _ptr(beta_log), _pdtype(alpha_log),
+                                   _ptr(y), y.stride(0), x.shape[0], x.shape[1], _stream(x.device)))
+    return y
+
+
+def channel_bias_add_t(x, bias, out=None):
+    import torch
+
+    _require_cuda(x, bias)
+    y = torch.empty_like(x) if out is None else out
+    check(lib().levo_channel_bias_add_f32(_ptr(x), _ptr(bias), _pdtype(bias), _ptr(y), x.shape[0], x.shape[1],
+                                          _stream(x.device)))
+    return y
+
+
+def fused_unit_t(u, bias=None, residual=None, alpha_log=None, beta_log=None, x_out=None, y_out=None,
+                 tanh=False, param_dtype=None):
+    _require_cuda(u, bias, residual, alpha_log, beta_log, x_out, y_out)
+    ref = next((t for t in (bias, alpha_log) if t is not None), None)
+    unit = FusedUnit(_ptr(u), _ptr(bias), _ptr(residual), _ptr(alpha_log), _ptr(beta_log), _ptr(x_out), _ptr(y_out),
+                     u.shape[0], u.shape[1],
+                     param_dtype if param_dtype is not None else (_pdtype(ref) if ref is not None else DTYPE_F32),
+                     FUSED_TANH if tanh else 0)
+    check(lib().levo_vae_fused_unit_f32(ctypes.byref(unit), _stream(u.device)))
+
+
+def _norm_call(name, x, r, gamma, beta, h_out, y_out, eps, flags):
+    _require_cuda(x, r, gamma, beta, h_out, y_out)
+    rows, dim = x.shape
+    args = [_ptr(x), _ptr(r), _ptr(gamma)]
+    if beta is not None or "layernorm" in name:
+        args.append(_ptr(beta))
+    args += [_ptr(h_out), _ptr(y_out), rows, dim, eps, flags, _stream(x.device)]
+    check(getattr(lib(), name)(*args))
+
+
+def add_rmsnorm_t(x, r, gamma, eps, f16_boundary=False, h_out=None, y_out=None):
+    """Returns (h, y): h = x + r, y = RMSNorm(h) * gamma; F16 or F32 activations."""
+    import torch
+
+    h = torch.empty_like(x) if (h_out is None and r is not None) else h_out
+    y = torch.empty_like(x) if y_out is None else y_out
+    name = "levo_add_rmsnorm_f16" if x.dtype == torch.float16 else "levo_add_rmsnorm_f32"
+    _norm_call(name, x, r, gamma, None, h, y, eps, NORM_F16_BOUNDARY if f16_boundary else 0)
+    return h, y
+
+
+def add_layernorm_t(x, r, gamma, beta, eps, f16_boundary=False, h_out=None, y_out=None):
+    import torch
+
+    h = torch.empty_like(x) if (h_out is None and r is not None) else h_out
+    y = torch.empty_like(x) if y_out is None else y_out
+    name = "levo_add_layernorm_f16" if x.dtype == torch.float16 else "levo_add_layernorm_f32"
+    _norm_call(name, x, r, gamma, beta, h, y, eps, NORM_F16_BOUNDARY if f16_boundary else 0)
+    return h, y
+
+
+def weightnorm_t(v, g, w=None, norms=None):
+    """w = v * (g / ||v||) per dim-0 row; v is [rows, ...] F32, g has one value per row."""
+    import torch
+
+    _require_cuda(v, g, w, norms)
+    rows = v.shape[0]
+    cols = v.numel() // max(rows, 1)
+    w = torch.empty_like(v) if w is None else w
+    check(lib().levo_weightnorm_f32(_ptr(v), _ptr(g), _ptr(w), _ptr(norms), rows, cols, _stream(v.device)))
+    return w
+
+
+def fold_weight_norm_t(v, g):
+    """Reference semantics of _fold_weight_norm (convert/convert_vae.py:187-199): raises on a zero norm."""
+    import torch
+
+    norms = torch.empty(v.shape[0], dtype=torch.float32, device=v.device)
+    w = weightnorm_t(v, g, norms=norms)
+    if bool((norms == 0).any().item()):
+        raise ValueError("zero weight-norm magnitude in weight_v")
+    return w
+
+
+def cfg_combine_t(uncond, cond, guidance, out=None):
+    import torch
+
+    _require_cuda(uncond, cond, out)
+    if uncond.numel() != cond.numel():
+        raise ValueError("CFG vectors must have equal non-empty lengths")
+    out = torch.empty_like(uncond) if out is None else out
+    check(lib().levo_cfg_combine_f32(_ptr(uncond), _ptr(cond), _ptr(out), uncond.numel(), guidance,
+                                     _stream(uncond.device)))
+    return out
+
+
+def flow_incontext_t(state, noise, context, prefix, step, steps, sigma_min, batch=1):
+    _require_cuda(state, noise, context)
+    row = state.numel() // batch
+    check(lib().levo_flow_incontext_f32(_ptr(state), _ptr(noise), _ptr(context), batch, row, prefix, step, steps,
+                                        sigma_min, _stream(state.device)))
+
+
+def euler_cfg_step_t(state, uncond, cond, guidance, steps, cfg=True, status=None):
+    _require_cuda(state, uncond, cond, status)
+    check(lib().levo_euler_cfg_step_f32(_ptr(state), _ptr(uncond), _ptr(cond), state.numel(), 1 if cfg else 0,
+                                        guidance, steps, _ptr(status), _stream(state.device)))
+
+
+def cfg_euler_multi_t(state, noise, context, uncond, cond, *, batch, prefix, first_step, count, steps,
+                      cfg=True, guidance=1.5, sigma_min=1e-4, status=None):
+    _require_cuda(state, noise, context, uncond, cond, status)
+    row = state.numel() // batch
+    check(lib().levo_cfg_euler_multi_f32(_ptr(state), _ptr(noise), _ptr(context), _ptr(uncond), _ptr(cond),
+                                         batch, row, prefix, first_step, count, steps, 1 if cfg else 0, guidance,
+                                         sigma_min, _ptr(status), _stream(state.device)))
+
+
+def reference_topology() -> Topology:
+    t = Topology()
+    check(lib().levo_vae_topology_reference(ctypes.byref(t)))
+    return t
+
+
+def param_count(topology: Topology) -> int:
+    n = lib().levo_vae_param_count(ctypes.byref(topology))
+    if n < 0:
+        check(int(n))
+    return int(n)
+
+
+class VaeChain:
+    """Owner of a levo_vae_chain (workspace + parameters on one device)."""
+
+    def __init__(self, topology: Topology, params_host, max_frames: int, device: int = 0, conv=None):
+        import numpy as np
+
+        self.topology = topology
+        self.params = np.ascontiguousarray(params_host, dtype=np.float32)
+        if self.params.size != param_count(topology):
+            raise ValueError("parameter array does not match the topology")
+        self._conv = CONV_FN(conv) if conv is not None else CONV_FN()
+        handle = ctypes.c_void_p()
+        check(lib().levo_vae_chain_create(ctypes.byref(handle), ctypes.byref(topology),
+                                          self.params.ctypes.data, max_frames, self._conv, None, device))
+        self.handle = handle
+        self.device = device
+        self.max_frames = max_frames
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().levo_vae_chain_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def samples(self, frames: int) -> int:
+        return frames * self.topology.upsampling()
+
+    def decode(self, latent, audio, frames: int, flags: int = 0, stream: Optional[int] = None) -> None:
+        """Device-resident decode: latent [latent_dim, frames] -> audio [channels, samples] (CUDA tensors)."""
+        check(lib().levo_vae_chain_decode(self.handle, _ptr(latent), frames, _ptr(audio), flags,
+                                          _stream(latent.device) if stream is None else stream))
+
+    def decode_windows(self, latents_host, audio_host, frames: int, flags: int = 0, cancel=None,
+                       stream: Optional[int] = None) -> None:
+        """Host-to-host decode of independent windows (numpy arrays or CPU tensors)."""
+        lat_ptr = latents_host.ctypes.data if hasattr(latents_host, "ctypes") else latents_host.data_ptr()
+        out_ptr = audio_host.ctypes.data if hasattr(audio_host, "ctypes") else audio_host.data_ptr()
+        windows = latents_host.shape[0]
+        cb = CANCEL_FN(lambda _u: 1 if cancel() else 0) if cancel is not None else CANCEL_FN()
+        if stream is None:
+            import torch
+
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib().levo_vae_chain_decode_windows(self.handle, lat_ptr, windows, frames, out_ptr, flags, cb, None,
+                                                  stream))
+
+    def timing(self, reset: bool = True) -> dict:
+        arr = (KernelTiming * len(KCLASS_NAMES))()
+        check(lib().levo_vae_chain_timing(self.handle, arr, 1 if reset else 0))
+        return {name: {"launches": arr[i].launches, "ms": arr[i].milliseconds,
+                       "bytes": arr[i].algorithmic_bytes, "elements": arr[i].elements}
+                for i, name in enumerate(KCLASS_NAMES)}

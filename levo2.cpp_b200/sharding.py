@@ -1,0 +1,112 @@
+"""Multi-GPU host logic for independent render windows.
+
+VAE windows are independent (the reference decodes them one after another,
+src/levo-render.cpp:442-451, src/cantor-abi.cpp:901-913), so N processes — one
+per GPU — each decode a contiguous block of windows with no collective on the
+data path.  The audio comes back to the host directly into one shared-memory
+buffer laid out [windows][channels][samples] (the host gather); rank 0 owns
+and finally unlinks it.  Collectives appear only for timing (a barrier and a
+max over ranks), never for data.
+"""
+from __future__ import annotations
+
+import os
+import tempfile
+from multiprocessing import shared_memory
+from typing import Callable, Optional
+
+import numpy as np
+
+
+def shard_range(n_items: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous block [start, stop) of n_items for `rank` out of `world` (sizes differ by <= 1)."""
+    if world <= 0 or not 0 <= rank < world or n_items < 0:
+        raise ValueError("invalid shard request")
+    base, extra = divmod(n_items, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+class HostGather:
+    """A [windows, channels, samples] F32 buffer in POSIX shared memory shared by the local ranks.
+
+    Rank 0 creates it before `barrier()`; the others attach after it.  `view(start, stop)` is
+    the slice a rank writes its own windows into.  `pin()` registers the mapping with CUDA so
+    device-to-host copies land in it by DMA.
+    """
+
+    def __init__(self, tag: str, shape: tuple[int, int, int], rank: int, barrier: Callable[[], None]):
+        self.shape = tuple(int(s) for s in shape)
+        self.nbytes = int(np.prod(self.shape)) * 4
+        self.rank = rank
+        self.name = f"levo_b200_{tag}"
+        self._pinned = False
+        self.shm = None
+        self.path = None
+        # POSIX shared memory when /dev/shm has room, else a file mapping in the temp dir.
+        use_shm = _free_bytes("/dev/shm") > self.nbytes * 1.1
+        if use_shm:
+            if rank == 0:
+                try:
+                    stale = shared_memory.SharedMemory(name=self.name)
+                    stale.close()
+                    stale.unlink()
+                except FileNotFoundError:
+                    pass
+                self.shm = shared_memory.SharedMemory(name=self.name, create=True, size=self.nbytes)
+            barrier()
+            if rank != 0:
+                self.shm = shared_memory.SharedMemory(name=self.name)
+            self.array = np.ndarray(self.shape, dtype=np.float32, buffer=self.shm.buf)
+        else:
+            self.path = os.path.join(tempfile.gettempdir(), self.name + ".f32")
+            if rank == 0:
+                self.array = np.memmap(self.path, dtype=np.float32, mode="w+", shape=self.shape)
+            barrier()
+            if rank != 0:
+                self.array = np.memmap(self.path, dtype=np.float32, mode="r+", shape=self.shape)
+
+    def view(self, start: int, stop: int) -> np.ndarray:
+        return self.array[start:stop]
+
+    def pin(self) -> bool:
+        """Page-locks the mapping for CUDA DMA; returns False when registration is refused."""
+        import torch
+
+        if self._pinned:
+            return True
+        rc = torch.cuda.cudart().cudaHostRegister(self.array.ctypes.data, self.nbytes, 0)
+        self._pinned = int(rc) == 0
+        return self._pinned
+
+    def close(self, barrier: Optional[Callable[[], None]] = None) -> None:
+        if self._pinned:
+            import torch
+
+            torch.cuda.cudart().cudaHostUnregister(self.array.ctypes.data)
+            self._pinned = False
+        self.array = None
+        if barrier is not None:
+            barrier()
+        if self.shm is not None:
+            self.shm.close()
+            if self.rank == 0:
+                try:
+                    self.shm.unlink()
+                except FileNotFoundError:
+                    pass
+        elif self.rank == 0 and self.path and os.path.exists(self.path):
+            os.unlink(self.path)
+
+
+def _free_bytes(path: str) -> int:
+    try:
+        st = os.statvfs(path)
+        return st.f_bavail * st.f_frsize
+    except OSError:
+        return 0
+
+
+def run_tag() -> str:
+    """A name shared by the ranks of one torchrun job (MASTER_PORT is common to them)."""
+    return f"{os.environ.get('MASTER_PORT', '0')}_{os.getppid() if os.environ.get('LOCAL_RANK') else os.getpid()}"

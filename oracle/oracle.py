@@ -1,0 +1,280 @@
+"""ctypes wrapper of the parity oracle (TEST INFRASTRUCTURE ONLY).
+
+liblevo_oracle.so is the C restatement (levo_oracle.c); _ref/libref_levo.so is
+the reference's own GGML-free renderer code (built only where the reference
+tree exists).  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline use this module, and only as the checker / the timed CPU baseline.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+from typing import Optional
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+ORACLE_LIB = HERE / "liblevo_oracle.so"
+REF_LIB = HERE / "_ref" / "libref_levo.so"
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_F = ctypes.c_float
+_INT = ctypes.c_int
+
+_SIGS = {
+    "oracle_snakebeta_f32": [_P, _P, _P, _P, _I64, _I64, _INT],
+    "oracle_snakebeta_f16params": [_P, _P, _P, _P, _I64, _I64, _INT],
+    "oracle_channel_bias_add_f32": [_P, _P, _P, _I64, _I64, _INT],
+    "oracle_fused_unit_f32": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _INT, _INT],
+    "oracle_conv_standin_f32": [_P, _I64, _I64, _P, _I64, _I64, _INT],
+    "oracle_vae_chain_f32": [_P, _P, _P, _I64, _P, _INT, _INT],
+    "oracle_add_rmsnorm_f16": [_P, _P, _P, _P, _P, _I64, _I64, _F, _INT, _INT],
+    "oracle_add_rmsnorm_f32": [_P, _P, _P, _P, _P, _I64, _I64, _F, _INT],
+    "oracle_add_layernorm_f16": [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _INT, _INT],
+    "oracle_add_layernorm_f32": [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _INT],
+    "oracle_weightnorm_f32": [_P, _P, _P, _P, _I64, _I64, _INT],
+    "oracle_cfg_combine_f32": [_P, _P, _P, _I64, _F],
+    "oracle_cfg_euler_f32": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _F, _F],
+}
+
+_REF_SIGS = {
+    "ref_last_error": (ctypes.c_char_p, []),
+    "ref_combine_renderer_cfg": (_INT, [_P, _P, _I64, _F, _P]),
+    "ref_solve_flow_euler": (_INT, [_P, _P, _I64, _I64, _I64, _F, _I64, _P, _P, _INT, _F, _I64, _P, _I64, _P, _P,
+                                    ctypes.POINTER(_I64)]),
+    "ref_make_renderer_schedule": (_INT, [_I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
+                                          _P, _I64]),
+    "ref_assemble_renderer_audio": (_INT, [_I64, _P, _P, _P, _P]),
+    "ref_make_renderer_euler_schedule": (_INT, [_I64, _P, ctypes.POINTER(_F)]),
+}
+
+_lib = None
+_ref = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not ORACLE_LIB.exists():
+            raise RuntimeError(f"{ORACLE_LIB} missing: run `make -C oracle`")
+        h = ctypes.CDLL(str(ORACLE_LIB))
+        for name, args in _SIGS.items():
+            fn = getattr(h, name)
+            fn.argtypes = args
+            fn.restype = None if name == "oracle_conv_standin_f32" else _INT
+        _lib = h
+    return _lib
+
+
+def ref_available() -> bool:
+    return REF_LIB.exists()
+
+
+def ref() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        if not REF_LIB.exists():
+            raise RuntimeError(f"{REF_LIB} missing: the reference tree was not present at build time")
+        h = ctypes.CDLL(str(REF_LIB))
+        for name, (res, args) in _REF_SIGS.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _ref = h
+    return _ref
+
+
+def _p(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# --------------------------------------------------------------------------- oracle (C restatement)
+
+def snakebeta(x, alpha_log, beta_log, threads: int = 0) -> np.ndarray:
+    x = _f32(x)
+    y = np.empty_like(x)
+    if np.asarray(alpha_log).dtype == np.float16:
+        a = np.ascontiguousarray(alpha_log, dtype=np.float16).view(np.uint16)
+        b = np.ascontiguousarray(beta_log, dtype=np.float16).view(np.uint16)
+        rc = lib().oracle_snakebeta_f16params(_p(x), _p(a), _p(b), _p(y), x.shape[0], x.shape[1], threads)
+    else:
+        a, b = _f32(alpha_log), _f32(beta_log)
+        rc = lib().oracle_snakebeta_f32(_p(x), _p(a), _p(b), _p(y), x.shape[0], x.shape[1], threads)
+    assert rc == 0
+    return y
+
+
+def channel_bias_add(x, bias, threads: int = 0) -> np.ndarray:
+    x, bias = _f32(x), _f32(bias)
+    y = np.empty_like(x)
+    assert lib().oracle_channel_bias_add_f32(_p(x), _p(bias), _p(y), x.shape[0], x.shape[1], threads) == 0
+    return y
+
+
+def fused_unit(u, bias=None, residual=None, alpha_log=None, beta_log=None, tanh=False, threads: int = 0):
+    """Returns (x, y) of the fused decoder unit expressed as separate reference nodes."""
+    u = _f32(u)
+    args = [None if a is None else _f32(a) for a in (bias, residual, alpha_log, beta_log)]
+    x = np.empty_like(u)
+    y = np.empty_like(u)
+    rc = lib().oracle_fused_unit_f32(_p(u), *[_p(a) for a in args], _p(x), _p(y), u.shape[0], u.shape[1],
+                                     1 if tanh else 0, threads)
+    assert rc == 0
+    return x, y
+
+
+def conv_standin(x, cout: int, lout: int, stride: int) -> np.ndarray:
+    x = _f32(x)
+    out = np.empty((cout, lout), dtype=np.float32)
+    lib().oracle_conv_standin_f32(_p(x), x.shape[0], x.shape[1], _p(out), cout, lout, stride)
+    return out
+
+
+def vae_chain(topology_list, params, latent, frames: int, audio_channels: int, samples: int, tanh=False,
+              threads: int = 0) -> np.ndarray:
+    topo = np.ascontiguousarray(topology_list, dtype=np.int32)
+    params, latent = _f32(params), _f32(latent)
+    audio = np.empty((audio_channels, samples), dtype=np.float32)
+    rc = lib().oracle_vae_chain_f32(_p(topo), _p(params), _p(latent), frames, _p(audio), 1 if tanh else 0, threads)
+    assert rc == 0
+    return audio
+
+
+def _norm(layer: bool, x, r, gamma, beta, eps, f16_boundary, threads):
+    half = x.dtype == np.float16
+    rows, dim = x.shape
+    gamma = _f32(gamma)
+    beta = _f32(beta) if beta is not None else None
+    if half:
+        xb = np.ascontiguousarray(x).view(np.uint16)
+        rb = None if r is None else np.ascontiguousarray(r, dtype=np.float16).view(np.uint16)
+        h = np.empty((rows, dim), np.uint16)
+        y = np.empty((rows, dim), np.uint16)
+        if layer:
+            rc = lib().oracle_add_layernorm_f16(_p(xb), _p(rb), _p(gamma), _p(beta), _p(h), _p(y), rows, dim, eps,
+                                                1 if f16_boundary else 0, threads)
+        else:
+            rc = lib().oracle_add_rmsnorm_f16(_p(xb), _p(rb), _p(gamma), _p(h), _p(y), rows, dim, eps,
+                                              1 if f16_boundary else 0, threads)
+        assert rc == 0
+        return h.view(np.float16), y.view(np.float16)
+    xf = _f32(x)
+    rf = None if r is None else _f32(r)
+    h = np.empty_like(xf)
+    y = np.empty_like(xf)
+    if layer:
+        rc = lib().oracle_add_layernorm_f32(_p(xf), _p(rf), _p(gamma), _p(beta), _p(h), _p(y), rows, dim, eps, threads)
+    else:
+        rc = lib().oracle_add_rmsnorm_f32(_p(xf), _p(rf), _p(gamma), _p(h), _p(y), rows, dim, eps, threads)
+    assert rc == 0
+    return h, y
+
+
+def add_rmsnorm(x, r, gamma, eps, f16_boundary=False, threads: int = 0):
+    return _norm(False, x, r, gamma, None, eps, f16_boundary, threads)
+
+
+def add_layernorm(x, r, gamma, beta, eps, f16_boundary=False, threads: int = 0):
+    return _norm(True, x, r, gamma, beta, eps, f16_boundary, threads)
+
+
+def weightnorm(v, g, threads: int = 0):
+    """Returns (w, norms, ok) where ok is False when a row norm is zero."""
+    v = _f32(v)
+    rows = v.shape[0]
+    cols = v.size // max(rows, 1)
+    g = _f32(g).reshape(-1)
+    w = np.empty_like(v)
+    norms = np.empty(rows, dtype=np.float32)
+    rc = lib().oracle_weightnorm_f32(_p(v), _p(g), _p(w), _p(norms), rows, cols, threads)
+    assert rc in (0, -1)
+    return w, norms, rc == 0
+
+
+def cfg_combine(u, c, g) -> np.ndarray:
+    u, c = _f32(u), _f32(c)
+    out = np.empty_like(u)
+    assert lib().oracle_cfg_combine_f32(_p(u), _p(c), _p(out), u.size, g) == 0
+    return out
+
+
+def cfg_euler(state, noise, context, uncond, cond, *, batch, prefix, first_step, count, steps, cfg=True,
+              guidance=1.5, sigma_min=1e-4):
+    """Returns (state_after, ok)."""
+    st = _f32(state).copy()
+    n = st.size
+    nz = _f32(noise) if noise is not None else np.zeros(n, np.float32)
+    cx = _f32(context) if context is not None else np.zeros(n, np.float32)
+    u = _f32(uncond) if uncond is not None else np.zeros(1, np.float32)
+    c = _f32(cond) if (cond is not None and cfg) else None
+    rc = lib().oracle_cfg_euler_f32(_p(st), _p(nz), _p(cx), _p(u), _p(c), batch, n // batch, prefix, first_step,
+                                    count, steps, 1 if cfg else 0, guidance, sigma_min)
+    assert rc in (0, -1)
+    return st, rc == 0
+
+
+# --------------------------------------------------------------------------- reference (compiled sources)
+
+def _ref_err() -> str:
+    m = ref().ref_last_error()
+    return m.decode() if m else ""
+
+
+def ref_combine_renderer_cfg(u, c, g) -> np.ndarray:
+    u, c = _f32(u), _f32(c)
+    out = np.empty_like(u)
+    if ref().ref_combine_renderer_cfg(_p(u), _p(c), u.size, g, _p(out)) != 0:
+        raise ValueError(_ref_err())
+    return out
+
+
+def ref_solve_flow_euler(noise, context, frames, latent_dim, incontext_frames, sigma_min, steps, uncond, cond,
+                         cfg=True, guidance=1.5, resume_step=-1, resume_state=None, pause_after=-1,
+                         want_seen=False):
+    """Returns (status, state, completed_steps, seen) — status 0 solved, 1 paused."""
+    n = frames * latent_dim
+    noise, context, uncond = _f32(noise), _f32(context), _f32(uncond)
+    cond = _f32(cond) if cond is not None else uncond
+    rs = _f32(resume_state) if resume_state is not None else None
+    seen = np.zeros((steps, n), np.float32) if want_seen else None
+    out = np.empty(n, np.float32)
+    done = _I64(0)
+    rc = ref().ref_solve_flow_euler(_p(noise), _p(context), frames, latent_dim, incontext_frames, sigma_min, steps,
+                                    _p(uncond), _p(cond), 1 if cfg else 0, guidance, resume_step, _p(rs),
+                                    pause_after, _p(seen), _p(out), ctypes.byref(done))
+    if rc < 0:
+        raise ValueError(_ref_err())
+    return rc, out, done.value, seen
+
+
+def ref_make_renderer_schedule(source_frames: int, max_windows: int = 4096):
+    pf, ts, nw = _I64(), _I64(), _I64()
+    desc = np.zeros((max_windows, 5), np.int64)
+    if ref().ref_make_renderer_schedule(source_frames, ctypes.byref(pf), ctypes.byref(ts), ctypes.byref(nw),
+                                        _p(desc), max_windows) != 0:
+        raise ValueError(_ref_err())
+    return {"padded_frames": pf.value, "target_samples": ts.value, "windows": desc[: nw.value].copy()}
+
+
+def ref_assemble_renderer_audio(source_frames: int, left, right):
+    sched = ref_make_renderer_schedule(source_frames)
+    left, right = _f32(left), _f32(right)
+    ol = np.empty(sched["target_samples"], np.float32)
+    orr = np.empty(sched["target_samples"], np.float32)
+    if ref().ref_assemble_renderer_audio(source_frames, _p(left), _p(right), _p(ol), _p(orr)) != 0:
+        raise ValueError(_ref_err())
+    return ol, orr
+
+
+def ref_make_renderer_euler_schedule(steps: int):
+    times = np.empty(steps + 1, np.float32)
+    dt = _F()
+    if ref().ref_make_renderer_euler_schedule(steps, _p(times), ctypes.byref(dt)) != 0:
+        raise ValueError(_ref_err())
+    return times, dt.value

@@ -1,0 +1,209 @@
+"""GPU parity of the decoder elementwise chain (a4) against the oracle's
+node-by-node restatement of src/levo-vae.cpp:212-235, through the C ABI.
+
+Convolutions use the built-in stand-ins on both sides (index-map copies for
+the input / upsample / output convs, identities for the residual convs).
+Tolerance: 1e-5 scaled error per sample (F32 path)."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def small_topology(ops, widths=((32, 4), (16, 3), (8, 2)), entry=64, latent=8, residual=2):
+    t = ops.Topology()
+    t.latent_dim, t.audio_channels, t.entry_width, t.n_stages = latent, 2, entry, len(widths)
+    for i, (w, s) in enumerate(widths):
+        t.stage_width[i], t.stage_stride[i] = w, s
+    t.n_residual = residual
+    for r in range(residual):
+        t.dilation[r] = 3 ** r
+    return t
+
+
+def params_for(ops, topo, seed):
+    rng = np.random.default_rng(seed)
+    return (0.1 * rng.standard_normal(ops.param_count(topo))).astype(np.float32)
+
+
+def oracle_audio(orc, topo, params, latent, frames, tanh=False):
+    return orc.vae_chain(topo.as_list(), params, latent, frames, topo.audio_channels, frames * topo.upsampling(),
+                         tanh=tanh)
+
+
+@pytest.mark.parametrize("frames", [1, 3, 20, 64])
+@pytest.mark.parametrize("tanh", [False, True])
+def test_small_chain_matches_oracle(ops, orc, dev, frames, tanh):
+    topo = small_topology(ops)
+    params = params_for(ops, topo, frames)
+    latent = np.random.default_rng(frames + 100).standard_normal((topo.latent_dim, frames)).astype(np.float32)
+    chain = ops.VaeChain(topo, params, max_frames=64, device=0)
+    audio = torch.full((2, chain.samples(frames)), np.nan, device=dev)
+    chain.decode(torch.from_numpy(latent).to(dev), audio, frames, flags=ops.CHAIN_TANH if tanh else 0)
+    assert_close(audio.cpu().numpy(), oracle_audio(orc, topo, params, latent, frames, tanh), TOL)
+    chain.close()
+
+
+@pytest.mark.parametrize("residual", [0, 1, 4])
+def test_chain_residual_counts(ops, orc, dev, residual):
+    topo = small_topology(ops, residual=residual)
+    params = params_for(ops, topo, 40 + residual)
+    frames = 9
+    latent = np.random.default_rng(residual).standard_normal((topo.latent_dim, frames)).astype(np.float32)
+    chain = ops.VaeChain(topo, params, max_frames=frames, device=0)
+    audio = torch.empty((2, chain.samples(frames)), device=dev)
+    chain.decode(torch.from_numpy(latent).to(dev), audio, frames)
+    assert_close(audio.cpu().numpy(), oracle_audio(orc, topo, params, latent, frames), TOL)
+
+
+@pytest.mark.parametrize("frames", [2, 8])
+def test_reference_topology_matches_oracle(ops, orc, dev, frames):
+    topo = ops.reference_topology()
+    params = params_for(ops, topo, 7)
+    latent = np.random.default_rng(8).standard_normal((64, frames)).astype(np.float32)
+    chain = ops.VaeChain(topo, params, max_frames=frames, device=0)
+    audio = torch.empty((2, frames * 1920), device=dev)
+    chain.decode(torch.from_numpy(latent).to(dev), audio, frames)
+    assert_close(audio.cpu().numpy(), oracle_audio(orc, topo, params, latent, frames), TOL)
+
+
+def test_reference_topology_full_window_properties(ops, dev):
+    # A 30 s window (T = 750): finite, tanh-bounded, deterministic across calls.
+    topo = ops.reference_topology()
+    params = params_for(ops, topo, 9)
+    frames = 750
+    latent = torch.from_numpy(np.random.default_rng(9).standard_normal((64, frames)).astype(np.float32)).to(dev)
+    chain = ops.VaeChain(topo, params, max_frames=frames, device=0)
+    a1 = torch.empty((2, frames * 1920), device=dev)
+    a2 = torch.empty_like(a1)
+    chain.decode(latent, a1, frames, flags=ops.CHAIN_TANH)
+    chain.decode(latent, a2, frames, flags=ops.CHAIN_TANH)
+    assert torch.isfinite(a1).all() and (a1.abs() <= 1).all()
+    assert torch.equal(a1, a2)
+    chain.close()
+
+
+def test_conv_callback_is_called_and_may_alias(ops, orc, dev):
+    """A user conv callback that reproduces the stand-ins with torch ops must give the same audio."""
+    topo = small_topology(ops)
+    params = params_for(ops, topo, 3)
+    frames = 6
+    latent = np.random.default_rng(3).standard_normal((topo.latent_dim, frames)).astype(np.float32)
+    seen = []
+    storage = {}
+
+    def as_tensor(ptr, c, l):
+        # wrap a device pointer as a torch tensor via a tiny cuda array interface
+        class Wrap:
+            __cuda_array_interface__ = {"shape": (c, l), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+        return torch.as_tensor(Wrap(), device=dev)
+
+    def conv(_user, call_p, _stream):
+        call = call_p.contents
+        seen.append(call.kind)
+        if call.kind in (ops.CONV_RES0, ops.CONV_RES1):
+            call.result = call.input  # identity: alias
+            return 0
+        src = as_tensor(call.input, call.in_channels, call.in_length)
+        dst = as_tensor(call.output, call.out_channels, call.out_length)
+        stride = call.stride if call.kind == ops.CONV_UPSAMPLE else 1
+        idx_c = torch.arange(call.out_channels, device=dev) % call.in_channels
+        idx_t = torch.arange(call.out_length, device=dev) // stride
+        dst.copy_(src[idx_c][:, idx_t])
+        storage["last"] = dst
+        return 0
+
+    chain = ops.VaeChain(topo, params, max_frames=frames, device=0, conv=conv)
+    audio = torch.empty((2, chain.samples(frames)), device=dev)
+    with torch.cuda.stream(torch.cuda.current_stream()):
+        chain.decode(torch.from_numpy(latent).to(dev), audio, frames)
+    torch.cuda.synchronize()
+    assert seen[0] == ops.CONV_INPUT and seen[-1] == ops.CONV_OUTPUT
+    assert seen.count(ops.CONV_UPSAMPLE) == topo.n_stages
+    assert seen.count(ops.CONV_RES0) == topo.n_stages * topo.n_residual
+    assert_close(audio.cpu().numpy(), oracle_audio(orc, topo, params, latent, frames), TOL)
+
+
+def test_conv_callback_failure_is_reported(ops, dev):
+    topo = small_topology(ops)
+    chain = ops.VaeChain(topo, params_for(ops, topo, 4), max_frames=4, device=0, conv=lambda u, c, s: 7)
+    audio = torch.empty((2, chain.samples(4)), device=dev)
+    with pytest.raises(ops.LevoOpsError, match="callback failed"):
+        chain.decode(torch.zeros((topo.latent_dim, 4), device=dev), audio, 4)
+
+
+def test_decode_windows_host_matches_device_decode(ops, dev):
+    topo = small_topology(ops)
+    params = params_for(ops, topo, 5)
+    frames, windows = 16, 5
+    lat = np.random.default_rng(5).standard_normal((windows, topo.latent_dim, frames)).astype(np.float32)
+    chain = ops.VaeChain(topo, params, max_frames=frames, device=0)
+    s = chain.samples(frames)
+    host = torch.empty((windows, 2, s), dtype=torch.float32).pin_memory()
+    chain.decode_windows(torch.from_numpy(lat).pin_memory(), host, frames, flags=ops.CHAIN_TANH)
+    pageable = np.empty((windows, 2, s), np.float32)
+    chain.decode_windows(lat, pageable, frames, flags=ops.CHAIN_TANH)
+    for w in range(windows):
+        d = torch.empty((2, s), device=dev)
+        chain.decode(torch.from_numpy(lat[w]).to(dev), d, frames, flags=ops.CHAIN_TANH)
+        torch.cuda.synchronize()
+        assert torch.equal(host[w], d.cpu())
+        assert np.array_equal(pageable[w], d.cpu().numpy())
+
+
+def test_decode_windows_cancel_between_windows(ops, dev):
+    # The reference polls cancellation between windows (src/cantor-abi.cpp:901-913).
+    topo = small_topology(ops)
+    chain = ops.VaeChain(topo, params_for(ops, topo, 6), max_frames=8, device=0)
+    lat = np.random.default_rng(6).standard_normal((4, topo.latent_dim, 8)).astype(np.float32)
+    out = np.full((4, 2, chain.samples(8)), np.nan, np.float32)
+    polls = []
+
+    def cancel():
+        polls.append(1)
+        return len(polls) > 2  # allow windows 0 and 1
+
+    with pytest.raises(ops.LevoCancelled, match="before window 2"):
+        chain.decode_windows(lat, out, 8, cancel=cancel)
+    assert np.all(np.isfinite(out[:2])) and np.all(np.isnan(out[2:]))
+
+
+def test_chain_timing_reports_every_class(ops, dev):
+    topo = ops.reference_topology()
+    chain = ops.VaeChain(topo, params_for(ops, topo, 10), max_frames=16, device=0)
+    lat = torch.randn((64, 16), device=dev)
+    audio = torch.empty((2, 16 * 1920), device=dev)
+    chain.decode(lat, audio, 16, flags=ops.CHAIN_TIMING | ops.CHAIN_TANH)
+    t = chain.timing()
+    assert t["entry"]["launches"] == 1 and t["upsample"]["launches"] == 5
+    assert t["post"]["launches"] == 15 and t["residual"]["launches"] == 15 and t["epilogue"]["launches"] == 1
+    assert t["conv"]["launches"] == 7  # input + 5 upsample + output stand-ins (residual convs alias)
+    assert all(v["ms"] > 0 for k, v in t.items())
+    # residual units move 16 B/elem except the last unit of each stage (12 B/elem)
+    elems = t["residual"]["elements"]
+    assert 12 * elems < t["residual"]["bytes"] < 16 * elems
+
+
+def test_chain_rejects_too_many_frames(ops, dev):
+    topo = small_topology(ops)
+    chain = ops.VaeChain(topo, params_for(ops, topo, 11), max_frames=4, device=0)
+    with pytest.raises(ValueError, match="max_frames"):
+        chain.decode(torch.zeros((topo.latent_dim, 5), device=dev), torch.zeros((2, 1000), device=dev), 5)
+
+
+def test_conv_standin(ops, orc, dev):
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((6, 11)).astype(np.float32)
+    out = torch.empty((4, 33), device=dev)
+    ops.check(ops.lib().levo_conv_standin_f32(torch.from_numpy(x).to(dev).data_ptr(), 6, 11, out.data_ptr(), 4, 33,
+                                              3, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    assert np.array_equal(out.cpu().numpy(), orc.conv_standin(x, 4, 33, 3))
