@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--no-kernels", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-tanh", action="store_true")
+    p.add_argument("--only-kernels", action="store_true",
+                   help="run only the configs 0-2 kernel suite (small; used for ncu captures)")
     return p.parse_args()
 
 
@@ -354,6 +356,14 @@ def kernel_suite(ops, dev, peak, steps, warmup):
     entry_("cfg_euler_f32[2,64,252]x50", timeit(
         lambda: ops.cfg_euler_multi_t(st, None, None, vu, vc, batch=2, prefix=0, first_step=0, count=S, steps=S,
                                       guidance=1.5)), 4 * n * (2 * S + 2), note="latency-bound: 13 MB")
+    # What a plain device copy of the same byte count reaches at these sizes (torch, not ours):
+    # the achievable ceiling for ~50 MB kernels, where launch and ramp-up are a large share.
+    for mb in (50, 496):
+        src = torch.empty(mb * 1024 * 1024 // 8, dtype=torch.float32, device=dev)
+        dst = torch.empty_like(src)
+        ms = timeit(lambda: dst.copy_(src))
+        out[f"torch_copy_{mb}MB_reference"] = {"ms": ms, "GB/s": 2 * src.numel() * 4 / (ms * 1e-3) / 1e9,
+                                              "frac": 2 * src.numel() * 4 / (ms * 1e-3) / 1e9 / peak}
     return out
 
 
@@ -493,10 +503,23 @@ def own_arm(args):
     return 0
 
 
+def only_kernels(args):
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ops = entry.load_package().ops
+    peak, _ = measured_peak()
+    print(json.dumps({"kernels": kernel_suite(ops, dev, peak, steps=args.steps, warmup=args.warmup)}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.only_kernels:
+        return only_kernels(args)
     return own_arm(args)
 
 

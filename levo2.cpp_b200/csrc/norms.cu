@@ -55,6 +55,15 @@ struct Act<__half> {
         }
         return w;
     }
+    // One 32-bit word = two values.
+    __device__ static float2 word(uint32_t w) {
+        return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+    }
+    __device__ static uint32_t make_word(float a, float b) {
+        const __half2 h2 = __floats2half2_rn(a, b);
+        return *reinterpret_cast<const uint32_t *>(&h2);
+    }
+    static constexpr int kPerWord = 2;
     __device__ static float load1(const void *p, int64_t i) {
         return __half2float(static_cast<const __half *>(p)[i]);
     }
@@ -76,6 +85,9 @@ struct Act<float> {
         for (int i = 0; i < 8; ++i) w.v[i] = __float_as_uint(in[i]);
         return w;
     }
+    __device__ static float2 word(uint32_t w) { return make_float2(__uint_as_float(w), 0.f); }
+    __device__ static uint32_t make_word(float a, float) { return __float_as_uint(a); }
+    static constexpr int kPerWord = 1;
     __device__ static float load1(const void *p, int64_t i) {
         return static_cast<const float *>(p)[i];
     }
@@ -114,9 +126,38 @@ __device__ __forceinline__ float norm_output(const NormArgs &a, float n, float g
     return y;
 }
 
+// Word-wise helpers: a 32-byte vector is 8 words of kPerWord values each; the
+// math touches one word (<= 2 values) at a time so only the packed row stays live.
+template <typename T>
+__device__ __forceinline__ float word_sum(uint32_t w, bool layer, float mean) {
+    const float2 f = Act<T>::word(w);
+    if (layer) {
+        const float d0 = __fsub_rn(f.x, mean);
+        float s = d0 * d0;
+        if (Act<T>::kPerWord == 2) {
+            const float d1 = __fsub_rn(f.y, mean);
+            s = fmaf(d1, d1, s);
+        }
+        return s;
+    }
+    float s = f.x * f.x;
+    if (Act<T>::kPerWord == 2) s = fmaf(f.y, f.y, s);
+    return s;
+}
+
+template <typename T>
+__device__ __forceinline__ float word_plain_sum(uint32_t w) {
+    const float2 f = Act<T>::word(w);
+    return Act<T>::kPerWord == 2 ? f.x + f.y : f.x;
+}
+
 template <typename T, int VPL, bool LAYER>
-__global__ void __launch_bounds__(kThreads) add_norm_vec_kernel(const NormArgs a) {
+// Rows of up to 96 bytes per thread are held to 64 registers (4 CTAs = 32 warps
+// per SM), enough for one wave of 4096 rows on 148 SMs.
+__global__ void __launch_bounds__(kThreads, (VPL * Act<T>::kVec * sizeof(T) <= 96) ? 4 : 1)
+    add_norm_vec_kernel(const NormArgs a) {
     constexpr int VE = Act<T>::kVec;
+    constexpr int PW = Act<T>::kPerWord;
     __shared__ float red[kThreads / 32];
     const int group_threads = 32 * a.wpr;
     const int groups = kThreads / group_threads;
@@ -130,7 +171,7 @@ __global__ void __launch_bounds__(kThreads) add_norm_vec_kernel(const NormArgs a
         const int64_t row = row0 + group;
         const bool active = row < a.rows;
         const size_t row_off = static_cast<size_t>(row) * a.dim * sizeof(T);
-        // hw holds the row in the activation type: h = x + r is exactly
+        // hw holds the row packed in the activation type: h = x + r is exactly
         // representable there, so the row costs 8 registers per vector.
         u32x8 hw[VPL], rw[VPL];
 #pragma unroll
@@ -146,17 +187,15 @@ __global__ void __launch_bounds__(kThreads) add_norm_vec_kernel(const NormArgs a
         for (int k = 0; k < VPL; ++k) {
             const int vi = k * group_threads + gl;
             if (active && vi < nvec) {
-                float h[VE];
-                Act<T>::unpack(hw[k], h);
-                if (a.r) {
-                    float rv[VE];
-                    Act<T>::unpack(rw[k], rv);
 #pragma unroll
-                    for (int i = 0; i < VE; ++i) h[i] = Act<T>::round(__fadd_rn(h[i], rv[i]));
-                    hw[k] = Act<T>::pack(h);
+                for (int i = 0; i < 8; ++i) {
+                    if (a.r) {
+                        const float2 x = Act<T>::word(hw[k].v[i]);
+                        const float2 r = Act<T>::word(rw[k].v[i]);
+                        hw[k].v[i] = Act<T>::make_word(__fadd_rn(x.x, r.x), __fadd_rn(x.y, r.y));
+                    }
+                    sum += LAYER ? word_plain_sum<T>(hw[k].v[i]) : word_sum<T>(hw[k].v[i], false, 0.f);
                 }
-#pragma unroll
-                for (int i = 0; i < VE; ++i) sum += LAYER ? h[i] : h[i] * h[i];
             }
         }
         sum = group_sum(sum, a.wpr, red);
@@ -168,13 +207,8 @@ __global__ void __launch_bounds__(kThreads) add_norm_vec_kernel(const NormArgs a
             for (int k = 0; k < VPL; ++k) {
                 const int vi = k * group_threads + gl;
                 if (active && vi < nvec) {
-                    float h[VE];
-                    Act<T>::unpack(hw[k], h);
 #pragma unroll
-                    for (int i = 0; i < VE; ++i) {
-                        const float d = __fsub_rn(h[i], mean);
-                        sq += d * d;
-                    }
+                    for (int i = 0; i < 8; ++i) sq += word_sum<T>(hw[k].v[i], true, mean);
                 }
             }
             sq = group_sum(sq, a.wpr, red);
@@ -189,21 +223,27 @@ __global__ void __launch_bounds__(kThreads) add_norm_vec_kernel(const NormArgs a
             if (vi >= nvec) continue;
             const int col = vi * VE;
             if (a.h_out && a.r) st8u(static_cast<char *>(a.h_out) + row_off + vi * 32, hw[k]);
-            float h[VE];
-            Act<T>::unpack(hw[k], h);
+            u32x8 yw;
 #pragma unroll
-            for (int i = 0; i < VE; i += 8) {
-                const f32x8 g = ld8_ro(a.gamma + col + i);
+            for (int i8 = 0; i8 < VE; i8 += 8) {
+                const f32x8 g = ld8_ro(a.gamma + col + i8);
                 f32x8 b{};
-                if (LAYER) b = ld8_ro(a.beta + col + i);
+                if (LAYER) b = ld8_ro(a.beta + col + i8);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float n = LAYER ? __fmul_rn(__fsub_rn(h[i + j], mean), scale)
-                                          : __fmul_rn(h[i + j], scale);
-                    h[i + j] = norm_output<T, LAYER>(a, n, g.v[j], b.v[j]);
+                for (int j = 0; j < 8 / PW; ++j) {
+                    const int wi = i8 / PW + j;
+                    const float2 h = Act<T>::word(hw[k].v[wi]);
+                    const float n0 = LAYER ? __fmul_rn(__fsub_rn(h.x, mean), scale) : __fmul_rn(h.x, scale);
+                    const float y0 = norm_output<T, LAYER>(a, n0, g.v[j * PW], b.v[j * PW]);
+                    float y1 = 0.f;
+                    if (PW == 2) {
+                        const float n1 = LAYER ? __fmul_rn(__fsub_rn(h.y, mean), scale) : __fmul_rn(h.y, scale);
+                        y1 = norm_output<T, LAYER>(a, n1, g.v[j * PW + 1], b.v[j * PW + 1]);
+                    }
+                    yw.v[wi] = Act<T>::make_word(y0, y1);
                 }
             }
-            st8u(static_cast<char *>(a.y_out) + row_off + vi * 32, Act<T>::pack(h));
+            st8u(static_cast<char *>(a.y_out) + row_off + vi * 32, yw);
         }
     }
 }
@@ -273,19 +313,19 @@ int run_norm(const char *what, const void *x, const void *r, const float *gamma,
              cudaStream_t stream) {
     clear_error();
     const std::string w(what);
-    if (x == nullptr || y_out == nullptr || gamma == nullptr || (LAYER && beta == nullptr))
-        return set_error(LEVO_OPS_EINVAL, w + ": required pointer is null");
     if (rows < 0 || dim < 0) return set_error(LEVO_OPS_EINVAL, w + ": negative shape");
     if (!(eps >= 0.f) || !std::isfinite(eps))
         return set_error(LEVO_OPS_EINVAL, w + ": eps must be finite and non-negative");
     if (flags & ~LEVO_NORM_F16_BOUNDARY) return set_error(LEVO_OPS_EINVAL, w + ": unknown flag bits");
     if ((flags & LEVO_NORM_F16_BOUNDARY) && sizeof(T) != 2)
         return set_error(LEVO_OPS_EINVAL, w + ": the F16 boundary flag needs F16 activations");
+    if (rows == 0 || dim == 0) return LEVO_OPS_OK;  // empty: nothing to read or write
+    if (x == nullptr || y_out == nullptr || gamma == nullptr || (LAYER && beta == nullptr))
+        return set_error(LEVO_OPS_EINVAL, w + ": required pointer is null");
     const void *ptrs[6] = {x, r, h_out, y_out, gamma, beta};
     for (int i = 0; i < 6; ++i)
         if (ptrs[i] && !aligned_to(ptrs[i], i < 4 ? sizeof(T) : 4))
             return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
-    if (rows == 0 || dim == 0) return LEVO_OPS_OK;
     if (dim > (1 << 20)) return set_error(LEVO_OPS_EUNSUPPORTED, w + ": dim above 1048576");
 
     NormArgs a{x, r, gamma, beta, h_out, y_out, rows, static_cast<int>(dim), 1, eps,

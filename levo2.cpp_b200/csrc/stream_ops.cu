@@ -38,7 +38,7 @@ struct StreamArgs {
 };
 
 struct ChannelParams {
-    float alpha, beta, bias;
+    float alpha, beta, bias;  // beta holds 1/beta
 };
 
 template <bool SNAKE>
@@ -54,7 +54,7 @@ __device__ __forceinline__ ChannelParams channel_params(const StreamArgs &a, con
     } else {
         if (SNAKE) {
             p.alpha = snake_alpha(load_param(a.alog, c, a.pdtype));
-            p.beta = snake_beta_den(load_param(a.blog, c, a.pdtype));
+            p.beta = snake_inv_beta(load_param(a.blog, c, a.pdtype));
         }
         if (a.has_bias) p.bias = load_param(a.bias, c, a.pdtype);
     }
@@ -94,7 +94,7 @@ __device__ __forceinline__ void stage_params(const StreamArgs &a, float *smem) {
     for (int64_t c = threadIdx.x; c < a.rows; c += blockDim.x) {
         if (SNAKE) {
             smem[c] = snake_alpha(load_param(a.alog, c, a.pdtype));
-            smem[a.rows + c] = snake_beta_den(load_param(a.blog, c, a.pdtype));
+            smem[a.rows + c] = snake_inv_beta(load_param(a.blog, c, a.pdtype));
         }
         if (a.has_bias) smem[2 * a.rows + c] = load_param(a.bias, c, a.pdtype);
     }
@@ -207,6 +207,8 @@ struct StreamRequest {
     int64_t ldy;
     int64_t rows, len;
     bool tanh_out;
+    bool need_snake;  // the entry point requires SnakeBeta parameters
+    bool need_bias;   // the entry point requires a bias
 };
 
 int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
@@ -214,7 +216,11 @@ int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
     if (q.rows < 0 || q.len < 0) return set_error(LEVO_OPS_EINVAL, w + ": negative shape");
     if (q.pdtype != LEVO_DTYPE_F32 && q.pdtype != LEVO_DTYPE_F16)
         return set_error(LEVO_OPS_EINVAL, w + ": parameter dtype must be F32 or F16");
+    if (q.rows == 0 || q.len == 0) return LEVO_OPS_OK;  // empty tensors: nothing to read or write
     if (q.u == nullptr) return set_error(LEVO_OPS_EINVAL, w + ": input is null");
+    if (q.need_snake && (q.alog == nullptr || q.blog == nullptr))
+        return set_error(LEVO_OPS_EINVAL, w + ": SnakeBeta parameters are null");
+    if (q.need_bias && q.bias == nullptr) return set_error(LEVO_OPS_EINVAL, w + ": bias is null");
     if ((q.alog == nullptr) != (q.blog == nullptr))
         return set_error(LEVO_OPS_EINVAL, w + ": alpha_log and beta_log must both be given");
     if (q.x_out == nullptr && q.y_out == nullptr)
@@ -228,7 +234,6 @@ int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
     for (int i = 0; i < 7; ++i)
         if (ptrs[i] && !aligned_to(ptrs[i], i < 4 ? 4 : pbytes))
             return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
-    if (q.rows == 0 || q.len == 0) return LEVO_OPS_OK;
     if (q.rows > (int64_t(1) << 40) / q.len)
         return set_error(LEVO_OPS_EINVAL, w + ": tensor too large");
 
@@ -311,10 +316,8 @@ LEVO_OPS_API int levo_snakebeta_f32(const float *x, int64_t ldx, const void *alp
                                     const void *beta_log, int param_dtype, float *y, int64_t ldy,
                                     int64_t channels, int64_t time, levo_stream_t stream) {
     levo::clear_error();
-    if (alpha_log == nullptr || beta_log == nullptr)
-        return levo::set_error(LEVO_OPS_EINVAL, "levo_snakebeta_f32: SnakeBeta parameters are null");
-    if (y == nullptr) return levo::set_error(LEVO_OPS_EINVAL, "levo_snakebeta_f32: output is null");
     levo::StreamRequest q{};
+    q.need_snake = true;
     q.u = x;
     q.ldu = ldx;
     q.alog = alpha_log;
@@ -331,11 +334,8 @@ LEVO_OPS_API int levo_channel_bias_add_f32(const float *in, const void *bias, in
                                            float *out, int64_t channels, int64_t time,
                                            levo_stream_t stream) {
     levo::clear_error();
-    if (bias == nullptr)
-        return levo::set_error(LEVO_OPS_EINVAL, "levo_channel_bias_add_f32: bias is null");
-    if (out == nullptr)
-        return levo::set_error(LEVO_OPS_EINVAL, "levo_channel_bias_add_f32: output is null");
     levo::StreamRequest q{};
+    q.need_bias = true;
     q.u = in;
     q.ldu = time;
     q.bias = bias;

@@ -44,6 +44,35 @@ __global__ void __launch_bounds__(256) conv_standin_kernel(const float *in, int6
     }
 }
 
+// Vector form for rows whose length is a multiple of 8 (32-byte aligned rows):
+// each thread writes 8 consecutive samples of one row with one 256-bit store;
+// the source index advances by one every `stride` samples.
+__global__ void __launch_bounds__(256) conv_standin_vec8_kernel(const float *in, int64_t cin,
+                                                               int64_t lin, float *out,
+                                                               int64_t cout, int64_t lout,
+                                                               int32_t stride, double inv_lout) {
+    const int64_t nvec = cout * lout / 8;
+    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
+         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = v * 8;
+        const int64_t c = row_of(e, lout, inv_lout);
+        const int64_t t0 = e - c * lout;
+        const float *src = in + (c % cin) * lin;
+        int64_t st = t0 / stride;
+        int32_t phase = static_cast<int32_t>(t0 - st * stride);
+        f32x8 o;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            o.v[k] = st < lin ? __ldg(src + st) : 0.f;
+            if (++phase == stride) {
+                phase = 0;
+                ++st;
+            }
+        }
+        st8(out + e, o);
+    }
+}
+
 struct SnakeRef {
     const float *alpha;
     const float *beta;
@@ -514,9 +543,17 @@ LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int
         return set_error(LEVO_OPS_EINVAL, "levo_conv_standin_f32: invalid shape or stride");
     const int64_t n = out_channels * out_length;
     if (n == 0) return LEVO_OPS_OK;
-    const int64_t grid = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
-    conv_standin_kernel<<<static_cast<unsigned>(grid), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        in, in_channels, in_length, out, out_channels, out_length, stride);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (out_length % 8 == 0 && aligned_to(out, 32)) {
+        const int64_t grid = std::min<int64_t>((n / 8 + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
+        conv_standin_vec8_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(
+            in, in_channels, in_length, out, out_channels, out_length, stride,
+            1.0 / static_cast<double>(out_length));
+    } else {
+        const int64_t grid = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
+        conv_standin_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(in, in_channels, in_length, out,
+                                                                     out_channels, out_length, stride);
+    }
     return check_launch("levo_conv_standin_f32");
 }
 

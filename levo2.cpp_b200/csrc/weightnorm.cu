@@ -121,14 +121,14 @@ LEVO_OPS_API int levo_weightnorm_f32(const float *v, const float *g, float *w, f
                                      int64_t rows, int64_t cols, levo_stream_t stream) {
     using namespace levo;
     clear_error();
+    if (rows < 0 || cols < 0) return set_error(LEVO_OPS_EINVAL, "levo_weightnorm_f32: negative shape");
+    if (rows == 0 || cols == 0) return LEVO_OPS_OK;  // empty: nothing to read or write
     if (v == nullptr || g == nullptr || w == nullptr)
         return set_error(LEVO_OPS_EINVAL, "levo_weightnorm_f32: required pointer is null");
-    if (rows < 0 || cols < 0) return set_error(LEVO_OPS_EINVAL, "levo_weightnorm_f32: negative shape");
     const void *ptrs[4] = {v, g, w, norms_out};
     for (const void *p : ptrs)
         if (p && !aligned_to(p, 4))
             return set_error(LEVO_OPS_EINVAL, "levo_weightnorm_f32: pointer is not 4-byte aligned");
-    if (rows == 0 || cols == 0) return LEVO_OPS_OK;
     const WnArgs a{v, g, w, norms_out, rows, cols};
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const bool vec = cols % 8 == 0 && aligned_to(v, 32) && aligned_to(w, 32);
