@@ -287,6 +287,22 @@ LEVO_OPS_API int levo_add_layernorm_f32(const float *x, const float *r, const fl
                                         int64_t rows, int64_t dim, float eps, uint32_t flags,
                                         levo_stream_t stream);
 
+/*
+ * Flow block form (next item f2): gated residual + LayerNorm + adaLN modulation
+ * in one pass over F32 [rows][dim], rows = batch * batch_rows:
+ *   h = r + x * gate[b]                               (src/levo-flow-estimator.cpp:221-227,243-246)
+ *   y = (LN(h) * gamma + beta) * (1 + scale[b]) + shift[b]
+ *                                                     (src/levo-flow-estimator.cpp:89-93,106-109,209-212)
+ * b = row / batch_rows; gate / scale / shift are [batch][dim] (the modulation
+ * chunks) and each may be NULL (no gate: h = r + x; r NULL: h = x * gate).
+ */
+LEVO_OPS_API int levo_gated_layernorm_modulate_f32(const float *x, const float *gate, const float *r,
+                                                   const float *gamma, const float *beta,
+                                                   const float *scale, const float *shift,
+                                                   int64_t batch_rows, float *h_out, float *y_out,
+                                                   int64_t rows, int64_t dim, float eps,
+                                                   levo_stream_t stream);
+
 /* ------------------------------------------------------------------------- */
 /* a9  weight-norm fold                                                       */
 /* ------------------------------------------------------------------------- */
@@ -355,6 +371,28 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
                                           int64_t first_step, int64_t count, int64_t steps,
                                           int32_t cfg, float guidance, float sigma_min,
                                           int32_t *status, levo_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* next (f1)  window assembly: crossfade + crop (+ interleave)                */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces assemble_renderer_audio (src/levo-renderer-pattern.cpp:137-203) and
+ * the L/R interleave of the render result (src/levo-render.cpp:476-480).
+ * windows: decoded windows [n_windows][channels][window_samples] (planar, as the
+ * decoder writes them).  Window k starts at k*hop_samples; the first
+ * overlap_samples of each window after the first are crossfaded linearly into
+ * what is already there (alpha = s / (overlap_samples - 1), previous * (1 - alpha)
+ * + current * alpha); the song is cropped to target_samples.
+ * out: planar [channels][target_samples] (interleaved == 0, the cantor ABI's
+ * [L..., R...] layout) or interleaved [target_samples][channels].
+ * Requires 2 <= overlap <= hop and hop + overlap <= window (or overlap == 0), as
+ * the reference's 750 / 250 / 1000-frame schedule satisfies.  Bit-identical to
+ * the reference (same F32 expression order).
+ */
+LEVO_OPS_API int levo_assemble_windows_f32(const float *windows, int64_t n_windows, int64_t channels,
+                                           int64_t window_samples, int64_t hop_samples,
+                                           int64_t overlap_samples, int64_t target_samples,
+                                           float *out, int32_t interleaved, levo_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -87,6 +87,19 @@ __device__ __forceinline__ void st8u(void *p, const u32x8 &r) {
 }
 
 // ---------------------------------------------------------------------------
+// Asynchronous global -> shared copies (cp.async, 16 bytes, L2 only).  The
+// wait is the hardware's cp.async.wait_all: no software spin loop.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(gmem_src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Parameters
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float load_param(const void *p, int64_t i, int dtype) {
@@ -108,18 +121,22 @@ __device__ __forceinline__ float snake_inv_beta(float beta_log) {
 // sin(t)^2, written for this library (no sinf call on the common path):
 //  1. Cody-Waite argument reduction (W. J. Cody, W. Waite, "Software Manual for
 //     the Elementary Functions", 1980): k = rint(t * 2/pi), r = t - k*pi/2 with
-//     pi/2 split into three F32 parts applied by FMA; |r| <= pi/4.
+//     pi/2 split into three F32 parts applied by FMA; |r| <= pi/4.  k is rounded
+//     by adding 1.5*2^23 (the sum's ulp is 1, so the FMA rounds t*2/pi to the
+//     nearest integer) and its parity is the sum's lowest mantissa bit.
 //  2. sin(t)^2 = sin(r)^2 for even k and 1 - sin(r)^2 for odd k.
 //  3. sin(r)^2 = z * Q(z), z = r^2, with Q a degree-5 polynomial fitted here by
 //     weighted least squares to sin(r)^2 / r^2 on [0, (pi/4)^2]
 //     (F32 relative error of z*Q(z) <= 1e-7; |error of sin^2| <= 1.2e-7 up to |t| = 1e5).
-// |t| > 65536 (and inf) takes CUDA's sinf, which carries its own large-argument reduction.
-__device__ __forceinline__ float sin_squared(float t) {
-    if (fabsf(t) > 65536.0f) {
-        const float s = sinf(t);
-        return s * s;
-    }
-    const float k = rintf(t * 0.636619747f);
+// Valid for |t| <= kSin2FastLimit; callers route larger (or infinite) arguments
+// to sin_squared_any(), which uses CUDA's sinf and its large-argument reduction.
+constexpr float kSin2FastLimit = 65536.0f;
+
+__device__ __forceinline__ float sin_squared_fast(float t) {
+    const float kBig = 12582912.0f;  // 1.5 * 2^23
+    const float ks = fmaf(t, 0.636619747f, kBig);
+    const int odd = __float_as_int(ks) & 1;
+    const float k = ks - kBig;
     float r = fmaf(-k, 1.57079637f, t);
     r = fmaf(-k, -4.37113883e-08f, r);
     r = fmaf(-k, -1.77635684e-15f, r);
@@ -130,11 +147,38 @@ __device__ __forceinline__ float sin_squared(float t) {
     q = fmaf(q, z, -3.333333433e-01f);
     q = fmaf(q, z, 1.0f);
     const float p = z * q;
-    return (__float2int_rn(k) & 1) ? 1.0f - p : p;
+    return odd ? 1.0f - p : p;
+}
+
+__device__ __forceinline__ float sin_squared_any(float t) {
+    if (fabsf(t) > kSin2FastLimit) {
+        const float s = sinf(t);
+        return s * s;
+    }
+    return sin_squared_fast(t);
 }
 
 __device__ __forceinline__ float snake_eval(float x, float alpha, float inv_beta) {
-    return __fmaf_rn(sin_squared(__fmul_rn(x, alpha)), inv_beta, x);
+    return __fmaf_rn(sin_squared_any(__fmul_rn(x, alpha)), inv_beta, x);
+}
+
+// SnakeBeta of 8 values of one channel: one range check per vector, then the
+// branch-free fast path (the common case) or the general one.
+__device__ __forceinline__ void snake_eval8(float (&v)[8], float alpha, float inv_beta) {
+    float t[8];
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        t[k] = __fmul_rn(v[k], alpha);
+        m = fmaxf(m, fabsf(t[k]));
+    }
+    if (m <= kSin2FastLimit) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __fmaf_rn(sin_squared_fast(t[k]), inv_beta, v[k]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __fmaf_rn(sin_squared_any(t[k]), inv_beta, v[k]);
+    }
 }
 
 // ---------------------------------------------------------------------------

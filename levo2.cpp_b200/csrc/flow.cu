@@ -186,6 +186,66 @@ __global__ void __launch_bounds__(kThreads) euler_multi_kernel(const MultiArgs a
     flag_status(a.status, bits);
 }
 
+// Staged form: a CTA of kStagedThreads threads owns kStagedThreads consecutive
+// elements; the velocities of up to kStagedSteps steps for them are copied into
+// shared memory with cp.async in one burst (all of config 2's 13 MB is in
+// flight at once), then each thread runs its steps from shared memory.
+constexpr int kStagedThreads = 64;
+constexpr int kStagedSteps = 64;
+
+__global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(const MultiArgs a) {
+    extern __shared__ float4 stage[];  // [2][steps][kStagedThreads/4] float4
+    const int64_t n = a.batch * a.row;
+    const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kStagedThreads;
+    const int64_t i = i0 + threadIdx.x;
+    const bool active = i < n;
+    const int per_step = kStagedThreads / 4;  // float4 chunks per step and array
+    const float dt = step_dt(a.steps);
+    int bits = 0;
+    const bool in_prefix = active && (i % a.row) < a.prefix;
+    float x = active ? a.state[i] : 0.f;
+    const float nz = in_prefix ? a.noise[i] : 0.f;
+    const float cx = in_prefix ? a.ctx[i] : 0.f;
+    const int64_t full = (n - i0) >= kStagedThreads ? per_step : (n - i0 + 3) / 4;
+    for (int64_t k0 = 0; k0 < a.count; k0 += kStagedSteps) {
+        const int cnt = static_cast<int>(a.count - k0 < kStagedSteps ? a.count - k0 : kStagedSteps);
+        __syncthreads();  // the previous chunk has been consumed
+        for (int idx = threadIdx.x; idx < 2 * cnt * per_step; idx += kStagedThreads) {
+            const int arr = idx / (cnt * per_step);
+            const int rem = idx - arr * cnt * per_step;
+            const int st = rem / per_step;
+            const int ch = rem - st * per_step;
+            if (ch < full && (arr == 0 || a.cfg)) {
+                const float *src = (arr == 0 ? a.u : a.c) + (k0 + st) * n + i0 + ch * 4;
+                cp_async16(stage + (arr * kStagedSteps + st) * per_step + ch, src);
+            }
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        if (active) {
+            const float *su = reinterpret_cast<const float *>(stage);
+            const float *sc = su + kStagedSteps * kStagedThreads;
+            for (int j = 0; j < cnt; ++j) {
+                if (in_prefix) {
+                    float t, ns;
+                    prefix_times(a.first + k0 + j, dt, a.sigma_min, t, ns);
+                    x = __fadd_rn(__fmul_rn(ns, nz), __fmul_rn(t, cx));
+                }
+                const float u = su[j * kStagedThreads + threadIdx.x];
+                const float v = a.cfg ? cfg_mix(u, sc[j * kStagedThreads + threadIdx.x], a.g) : u;
+                if (!isfinite(v)) bits |= 1;
+                x = __fadd_rn(x, __fmul_rn(dt, v));
+                if (!isfinite(x)) bits |= 2;
+            }
+        }
+    }
+    if (active) {
+        if (in_prefix && a.first + a.count == a.steps) x = cx;
+        a.state[i] = x;
+    }
+    flag_status(a.status, bits);
+}
+
 int64_t grid_for(int64_t items) {
     return std::max<int64_t>(
         1, std::min<int64_t>((items + kThreads - 1) / kThreads, static_cast<int64_t>(sm_count()) * 16));
@@ -296,8 +356,17 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
             return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: pointer is not 4-byte aligned");
     const MultiArgs a{state, noise, context, uncond, cond, batch, row, prefix, first_step,
                       count, steps, cfg ? 1 : 0, guidance, sigma_min, status};
-    euler_multi_kernel<<<static_cast<unsigned>(grid_for(batch * row)), kThreads, 0,
-                         reinterpret_cast<cudaStream_t>(stream)>>>(a);
+    const int64_t n = batch * row;
+    const bool staged = count > 0 && n % 4 == 0 && aligned_to(uncond, 16) && (!cfg || aligned_to(cond, 16));
+    if (staged) {
+        // [2][kStagedSteps][kStagedThreads] F32 = 32 KB of shared memory
+        const size_t smem = 2 * kStagedSteps * kStagedThreads * sizeof(float);
+        euler_multi_staged_kernel<<<static_cast<unsigned>((n + kStagedThreads - 1) / kStagedThreads),
+                                    kStagedThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+    } else {
+        euler_multi_kernel<<<static_cast<unsigned>(grid_for(n)), kThreads, 0,
+                             reinterpret_cast<cudaStream_t>(stream)>>>(a);
+    }
     return check_launch("levo_cfg_euler_multi_f32");
 }
 

@@ -29,6 +29,11 @@ struct NormArgs {
     int wpr;  // warps per row (vector path)
     float eps;
     int f16_boundary;
+    // Flow adaLN form (MOD kernels only): per-batch [rows / batch_rows][dim] F32 vectors.
+    const float *gate;   // h = r + x * gate       (src/levo-flow-estimator.cpp:221-227)
+    const float *scale;  // y = y * (1 + scale) + shift (src/levo-flow-estimator.cpp:89-93)
+    const float *shift;
+    int64_t batch_rows;
 };
 
 template <typename T>
@@ -126,6 +131,13 @@ __device__ __forceinline__ float norm_output(const NormArgs &a, float n, float g
     return y;
 }
 
+// add_scale_shift (src/levo-flow-estimator.cpp:89-93): y * (scale*1 + 1) + shift.
+__device__ __forceinline__ float modulate(const NormArgs &a, float y, float s, float sh) {
+    if (a.scale) y = __fmul_rn(y, __fadd_rn(s, 1.0f));
+    if (a.shift) y = __fadd_rn(y, sh);
+    return y;
+}
+
 // Word-wise helpers: a 32-byte vector is 8 words of kPerWord values each; the
 // math touches one word (<= 2 values) at a time so only the packed row stays live.
 template <typename T>
@@ -151,10 +163,11 @@ __device__ __forceinline__ float word_plain_sum(uint32_t w) {
     return Act<T>::kPerWord == 2 ? f.x + f.y : f.x;
 }
 
-template <typename T, int VPL, bool LAYER>
-// Rows of up to 96 bytes per thread are held to 64 registers (4 CTAs = 32 warps
-// per SM), enough for one wave of 4096 rows on 148 SMs.
-__global__ void __launch_bounds__(kThreads, (VPL * Act<T>::kVec * sizeof(T) <= 96) ? 4 : 1)
+template <typename T, int VPL, bool LAYER, bool MOD>
+// RMSNorm rows of up to 96 bytes per thread are held to 64 registers (4 CTAs =
+// 32 warps per SM, one wave of 4096 rows on 148 SMs).  LayerNorm keeps its
+// registers: the same cap spills its two-pass variance.
+__global__ void __launch_bounds__(kThreads, (!LAYER && !MOD && VPL * Act<T>::kVec * sizeof(T) <= 96) ? 4 : 1)
     add_norm_vec_kernel(const NormArgs a) {
     constexpr int VE = Act<T>::kVec;
     constexpr int PW = Act<T>::kPerWord;
@@ -171,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, (VPL * Act<T>::kVec * sizeof(T) <= 9
         const int64_t row = row0 + group;
         const bool active = row < a.rows;
         const size_t row_off = static_cast<size_t>(row) * a.dim * sizeof(T);
+        const int64_t mod_off = MOD ? (row / a.batch_rows) * a.dim : 0;
         // hw holds the row packed in the activation type: h = x + r is exactly
         // representable there, so the row costs 8 registers per vector.
         u32x8 hw[VPL], rw[VPL];
@@ -187,15 +201,34 @@ __global__ void __launch_bounds__(kThreads, (VPL * Act<T>::kVec * sizeof(T) <= 9
         for (int k = 0; k < VPL; ++k) {
             const int vi = k * group_threads + gl;
             if (active && vi < nvec) {
+                if (MOD && a.gate) {
+                    // h = r + x * gate, one gate value per column of this row's batch
+                    const float *gp = a.gate + mod_off + vi * VE;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    if (a.r) {
+                    for (int i8 = 0; i8 < VE; i8 += 8) {
+                        const f32x8 g = ld8_ro(gp + i8);
+#pragma unroll
+                        for (int j = 0; j < 8 / PW; ++j) {
+                            const int wi = i8 / PW + j;
+                            const float2 x = Act<T>::word(hw[k].v[wi]);
+                            const float2 r = a.r ? Act<T>::word(rw[k].v[wi]) : make_float2(0.f, 0.f);
+                            const float h0 = __fmul_rn(x.x, g.v[j * PW]);
+                            const float h1 = PW == 2 ? __fmul_rn(x.y, g.v[j * PW + 1]) : 0.f;
+                            hw[k].v[wi] = a.r ? Act<T>::make_word(__fadd_rn(h0, r.x), __fadd_rn(h1, r.y))
+                                              : Act<T>::make_word(h0, h1);
+                        }
+                    }
+                } else if (a.r) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
                         const float2 x = Act<T>::word(hw[k].v[i]);
                         const float2 r = Act<T>::word(rw[k].v[i]);
                         hw[k].v[i] = Act<T>::make_word(__fadd_rn(x.x, r.x), __fadd_rn(x.y, r.y));
                     }
-                    sum += LAYER ? word_plain_sum<T>(hw[k].v[i]) : word_sum<T>(hw[k].v[i], false, 0.f);
                 }
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    sum += LAYER ? word_plain_sum<T>(hw[k].v[i]) : word_sum<T>(hw[k].v[i], false, 0.f);
             }
         }
         sum = group_sum(sum, a.wpr, red);
@@ -222,23 +255,28 @@ __global__ void __launch_bounds__(kThreads, (VPL * Act<T>::kVec * sizeof(T) <= 9
             const int vi = k * group_threads + gl;
             if (vi >= nvec) continue;
             const int col = vi * VE;
-            if (a.h_out && a.r) st8u(static_cast<char *>(a.h_out) + row_off + vi * 32, hw[k]);
+            if (a.h_out && (a.r || (MOD && a.gate)))
+                st8u(static_cast<char *>(a.h_out) + row_off + vi * 32, hw[k]);
             u32x8 yw;
 #pragma unroll
             for (int i8 = 0; i8 < VE; i8 += 8) {
                 const f32x8 g = ld8_ro(a.gamma + col + i8);
-                f32x8 b{};
+                f32x8 b{}, ms{}, mh{};
                 if (LAYER) b = ld8_ro(a.beta + col + i8);
+                if (MOD && a.scale) ms = ld8_ro(a.scale + mod_off + col + i8);
+                if (MOD && a.shift) mh = ld8_ro(a.shift + mod_off + col + i8);
 #pragma unroll
                 for (int j = 0; j < 8 / PW; ++j) {
                     const int wi = i8 / PW + j;
                     const float2 h = Act<T>::word(hw[k].v[wi]);
                     const float n0 = LAYER ? __fmul_rn(__fsub_rn(h.x, mean), scale) : __fmul_rn(h.x, scale);
-                    const float y0 = norm_output<T, LAYER>(a, n0, g.v[j * PW], b.v[j * PW]);
+                    float y0 = norm_output<T, LAYER>(a, n0, g.v[j * PW], b.v[j * PW]);
+                    if (MOD) y0 = modulate(a, y0, ms.v[j * PW], mh.v[j * PW]);
                     float y1 = 0.f;
                     if (PW == 2) {
                         const float n1 = LAYER ? __fmul_rn(__fsub_rn(h.y, mean), scale) : __fmul_rn(h.y, scale);
                         y1 = norm_output<T, LAYER>(a, n1, g.v[j * PW + 1], b.v[j * PW + 1]);
+                        if (MOD) y1 = modulate(a, y1, ms.v[j * PW + 1], mh.v[j * PW + 1]);
                     }
                     yw.v[wi] = Act<T>::make_word(y0, y1);
                 }
@@ -255,9 +293,16 @@ __global__ void __launch_bounds__(kThreads) add_norm_scalar_kernel(const NormArg
     const float inv_dim = 1.0f / static_cast<float>(a.dim);
     for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
         const int64_t base = row * a.dim;
+        const int64_t mod_off = a.batch_rows > 0 ? (row / a.batch_rows) * a.dim : 0;
         auto hval = [&](int j) {
             float v = Act<T>::load1(a.x, base + j);
-            if (a.r) v = Act<T>::round(__fadd_rn(v, Act<T>::load1(a.r, base + j)));
+            if (a.gate) {
+                v = __fmul_rn(v, a.gate[mod_off + j]);
+                if (a.r) v = __fadd_rn(v, Act<T>::load1(a.r, base + j));
+                v = Act<T>::round(v);
+            } else if (a.r) {
+                v = Act<T>::round(__fadd_rn(v, Act<T>::load1(a.r, base + j)));
+            }
             return v;
         };
         float sum = 0.f;
@@ -291,26 +336,28 @@ __global__ void __launch_bounds__(kThreads) add_norm_scalar_kernel(const NormArg
         }
         for (int j = threadIdx.x; j < a.dim; j += kThreads) {
             const float v = hval(j);
-            if (a.h_out && a.r) Act<T>::store1(a.h_out, base + j, v);
+            if (a.h_out && (a.r || a.gate)) Act<T>::store1(a.h_out, base + j, v);
             const float n = LAYER ? __fmul_rn(__fsub_rn(v, mean), scale) : __fmul_rn(v, scale);
-            Act<T>::store1(a.y_out, base + j,
-                           norm_output<T, LAYER>(a, n, a.gamma[j], LAYER ? a.beta[j] : 0.f));
+            float y = norm_output<T, LAYER>(a, n, a.gamma[j], LAYER ? a.beta[j] : 0.f);
+            y = modulate(a, y, a.scale ? a.scale[mod_off + j] : 0.f, a.shift ? a.shift[mod_off + j] : 0.f);
+            Act<T>::store1(a.y_out, base + j, y);
         }
     }
 }
 
-template <typename T, int VPL, bool LAYER>
+template <typename T, int VPL, bool LAYER, bool MOD>
 void launch_vec(const NormArgs &a, cudaStream_t stream) {
     const int groups = kThreads / (32 * a.wpr);
     const int64_t grid = std::min<int64_t>((a.rows + groups - 1) / groups,
                                            static_cast<int64_t>(sm_count()) * 64);
-    add_norm_vec_kernel<T, VPL, LAYER><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(a);
+    add_norm_vec_kernel<T, VPL, LAYER, MOD><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(a);
 }
 
-template <typename T, bool LAYER>
+template <typename T, bool LAYER, bool MOD = false>
 int run_norm(const char *what, const void *x, const void *r, const float *gamma, const float *beta,
              void *h_out, void *y_out, int64_t rows, int64_t dim, float eps, uint32_t flags,
-             cudaStream_t stream) {
+             cudaStream_t stream, const float *gate = nullptr, const float *mscale = nullptr,
+             const float *mshift = nullptr, int64_t batch_rows = 0) {
     clear_error();
     const std::string w(what);
     if (rows < 0 || dim < 0) return set_error(LEVO_OPS_EINVAL, w + ": negative shape");
@@ -328,22 +375,35 @@ int run_norm(const char *what, const void *x, const void *r, const float *gamma,
             return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
     if (dim > (1 << 20)) return set_error(LEVO_OPS_EUNSUPPORTED, w + ": dim above 1048576");
 
+    if (MOD && (batch_rows <= 0 || rows % batch_rows != 0))
+        return set_error(LEVO_OPS_EINVAL, w + ": batch_rows must be positive and divide rows");
+    const void *mods[3] = {gate, mscale, mshift};
+    for (const void *m : mods)
+        if (m && !aligned_to(m, 4))
+            return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
     NormArgs a{x, r, gamma, beta, h_out, y_out, rows, static_cast<int>(dim), 1, eps,
-               (flags & LEVO_NORM_F16_BOUNDARY) ? 1 : 0};
+               (flags & LEVO_NORM_F16_BOUNDARY) ? 1 : 0, gate, mscale, mshift, MOD ? batch_rows : 0};
     constexpr int VE = Act<T>::kVec;
     constexpr int kMaxVpl = sizeof(T) == 2 ? 4 : 8;  // <= 64 F32 values per thread
     bool vec = (dim * sizeof(T)) % 32 == 0 && (dim % 8 == 0);
     for (int i = 0; i < 6 && vec; ++i)
         if (ptrs[i] && !aligned_to(ptrs[i], 32)) vec = false;
+    for (const void *m : mods)
+        if (m && !aligned_to(m, 32)) vec = false;
     int vpl = 0;
     if (vec) {
         const int nvec = static_cast<int>(dim / VE);
-        for (int wpr = 1; wpr <= 8; wpr *= 2) {
-            const int need = (nvec + 32 * wpr - 1) / (32 * wpr);
-            if (need <= kMaxVpl) {
-                a.wpr = wpr;
-                vpl = need;
-                break;
+        // Fewest warps per row whose share fits the register budget; prefer
+        // <= 3 vectors per thread (lean registers) when a wider group allows it.
+        for (int pass = 0; pass < 2 && vpl == 0; ++pass) {
+            const int limit = pass == 0 ? 3 : kMaxVpl;
+            for (int wpr = 1; wpr <= 8; wpr *= 2) {
+                const int need = (nvec + 32 * wpr - 1) / (32 * wpr);
+                if (need <= limit) {
+                    a.wpr = wpr;
+                    vpl = need;
+                    break;
+                }
             }
         }
         if (vpl == 0) vec = false;
@@ -352,16 +412,16 @@ int run_norm(const char *what, const void *x, const void *r, const float *gamma,
         // Instantiated vectors-per-thread: 1,2,3,4 (+6,8 for F32); a larger
         // count than needed is masked per vector.
         if (vpl == 1) {
-            launch_vec<T, 1, LAYER>(a, stream);
+            launch_vec<T, 1, LAYER, MOD>(a, stream);
         } else if (vpl == 2) {
-            launch_vec<T, 2, LAYER>(a, stream);
+            launch_vec<T, 2, LAYER, MOD>(a, stream);
         } else if (vpl == 3) {
-            launch_vec<T, 3, LAYER>(a, stream);
+            launch_vec<T, 3, LAYER, MOD>(a, stream);
         } else if (vpl == 4) {
-            launch_vec<T, 4, LAYER>(a, stream);
+            launch_vec<T, 4, LAYER, MOD>(a, stream);
         } else if constexpr (sizeof(T) == 4) {
-            if (vpl <= 6) launch_vec<T, 6, LAYER>(a, stream);
-            else launch_vec<T, 8, LAYER>(a, stream);
+            if (vpl <= 6) launch_vec<T, 6, LAYER, MOD>(a, stream);
+            else launch_vec<T, 8, LAYER, MOD>(a, stream);
         }
     } else {
         const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * 8);
@@ -398,6 +458,18 @@ LEVO_OPS_API int levo_add_layernorm_f16(const void *x, const void *r, const floa
     return levo::run_norm<__half, true>("levo_add_layernorm_f16", x, r, gamma, beta, h_out, y_out,
                                         rows, dim, eps, flags,
                                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+LEVO_OPS_API int levo_gated_layernorm_modulate_f32(const float *x, const float *gate, const float *r,
+                                                   const float *gamma, const float *beta,
+                                                   const float *scale, const float *shift,
+                                                   int64_t batch_rows, float *h_out, float *y_out,
+                                                   int64_t rows, int64_t dim, float eps,
+                                                   levo_stream_t stream) {
+    return levo::run_norm<float, true, true>("levo_gated_layernorm_modulate_f32", x, r, gamma, beta, h_out,
+                                             y_out, rows, dim, eps, 0,
+                                             reinterpret_cast<cudaStream_t>(stream), gate, scale, shift,
+                                             batch_rows);
 }
 
 LEVO_OPS_API int levo_add_layernorm_f32(const float *x, const float *r, const float *gamma,

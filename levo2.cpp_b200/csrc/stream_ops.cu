@@ -1,13 +1,18 @@
 // Streaming elementwise kernels over dense [channels][time] F32 tensors:
 // SnakeBeta (a1), per-channel bias add (a2) and the fused decoder unit (a3).
 //
-// One kernel template serves all three.  Each is a single HBM pass: every
-// input element is read once with a 256-bit load and every output written
-// once with a 256-bit store.  Per-channel parameters (alpha, beta, bias) are
-// promoted to F32, exponentiated and staged in shared memory once per CTA.
-// The grid is persistent (a multiple of the SM count) and walks the flat
-// element space in tiles; a vector that straddles a row boundary selects its
-// parameters per element.
+// Each is a single HBM pass: every input element is read once with a 256-bit
+// load and every output written once with a 256-bit store.  Two vector forms:
+//  * rows form (rows of a multiple of 8 values, 32-byte aligned tensors, the
+//    decoder's case): the tensor is cut into row chunks of kThreads*UNROLL
+//    vectors; each CTA of the persistent grid walks one contiguous range of
+//    chunks, so the channel is uniform per chunk and its parameters (alpha,
+//    1/beta, bias: promoted to F32 and exponentiated) are recomputed in
+//    registers only when the range crosses into the next row.
+//  * flat form (any row length, any common 32-byte phase): the flat element
+//    space is walked in tiles with parameters staged in shared memory once per
+//    CTA; a vector that straddles a row boundary selects them per element.
+// A scalar form covers strided rows and mismatched alignments.
 #include <algorithm>
 #include <cmath>
 
@@ -35,6 +40,11 @@ struct StreamArgs {
     double inv_len;
     int pdtype;
     int has_bias, write_x, write_y, tanh_out, staged;
+    // rows form
+    int64_t vec_per_row;  // len / 8
+    int64_t chunks_per_row;
+    int64_t chunks;       // rows * chunks_per_row
+    double inv_chunks_per_row;
 };
 
 struct ChannelParams {
@@ -72,6 +82,65 @@ __device__ __forceinline__ void unit_eval(const StreamArgs &a, const ChannelPara
     if (SNAKE) w = snake_eval(v, p.alpha, p.beta);
     if (a.tanh_out) w = tanhf(w);
     y = w;
+}
+
+// 8 values of one channel: bias, residual, SnakeBeta (one range check per
+// vector), tanh.  x keeps the pre-activation sum, y the activation.
+template <bool HAS_RES, bool SNAKE>
+__device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelParams &p, const f32x8 &u,
+                                           const f32x8 &r, f32x8 &x, f32x8 &y) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        float v = u.v[k];
+        if (a.has_bias) v = __fadd_rn(v, p.bias);
+        if (HAS_RES) v = __fadd_rn(r.v[k], v);
+        x.v[k] = v;
+        y.v[k] = v;
+    }
+    if (SNAKE) snake_eval8(y.v, p.alpha, p.beta);
+    if (a.tanh_out) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y.v[k] = tanhf(y.v[k]);
+    }
+}
+
+// Rows form: CTA b owns chunks [b*chunks/G, (b+1)*chunks/G); chunk q covers
+// vectors [k*kThreads*UNROLL, (k+1)*kThreads*UNROLL) of row c, q = c*cpr + k.
+template <bool HAS_RES, bool SNAKE, int UNROLL>
+__global__ void __launch_bounds__(kThreads) stream_rows_kernel(const StreamArgs a) {
+    const int64_t q0 = a.chunks * blockIdx.x / gridDim.x;
+    const int64_t q1 = a.chunks * (blockIdx.x + 1) / gridDim.x;
+    if (q0 >= q1) return;
+    int64_t c = row_of(q0, a.chunks_per_row, a.inv_chunks_per_row);
+    int64_t k = q0 - c * a.chunks_per_row;
+    ChannelParams p = channel_params<SNAKE>(a, nullptr, c);
+    for (int64_t q = q0; q < q1; ++q) {
+        const size_t row = static_cast<size_t>(c) * a.len;
+        const int64_t v0 = k * (kThreads * UNROLL) + threadIdx.x;
+        f32x8 uu[UNROLL], rr[UNROLL];
+#pragma unroll
+        for (int j = 0; j < UNROLL; ++j) {
+            const int64_t v = v0 + j * kThreads;
+            if (v < a.vec_per_row) {
+                uu[j] = ld8(a.u + row + v * 8);
+                if (HAS_RES) rr[j] = ld8(a.res + row + v * 8);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < UNROLL; ++j) {
+            const int64_t v = v0 + j * kThreads;
+            if (v >= a.vec_per_row) continue;
+            f32x8 xo, yo;
+            unit_eval8<HAS_RES, SNAKE>(a, p, uu[j], rr[j], xo, yo);
+            if (a.write_x) st8(a.x_out + row + v * 8, xo);
+            if (a.write_y) st8(a.y_out + row + v * 8, yo);
+        }
+        if (++k == a.chunks_per_row && q + 1 < q1) {
+            k = 0;
+            ++c;
+            p = channel_params<SNAKE>(a, nullptr, c);
+        }
+    }
 }
 
 // Scalar element e with per-tensor row strides.
@@ -140,10 +209,7 @@ __global__ void __launch_bounds__(kThreads) stream_vec8_kernel(const StreamArgs 
                 const int64_t boundary = (c0 + 1) * a.len;
                 const ChannelParams p0 = channel_params<SNAKE>(a, smem, c0);
                 if (e + 8 <= boundary) {
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        unit_eval<HAS_RES, SNAKE>(a, p0, uu[j].v[k], HAS_RES ? rr[j].v[k] : 0.f,
-                                                  xo.v[k], yo.v[k]);
+                    unit_eval8<HAS_RES, SNAKE>(a, p0, uu[j], rr[j], xo, yo);
                 } else {
                     const ChannelParams p1 = channel_params<SNAKE>(a, smem, c0 + 1);
 #pragma unroll
@@ -174,6 +240,24 @@ __global__ void __launch_bounds__(kThreads) stream_scalar_kernel(const StreamArg
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < a.n;
          e += static_cast<int64_t>(gridDim.x) * blockDim.x)
         scalar_element<HAS_RES, SNAKE>(a, smem, e);
+}
+
+template <bool HAS_RES, bool SNAKE>
+int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
+    constexpr int kRowUnroll = HAS_RES ? 2 : 4;
+    auto kernel = stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll>;
+    a.staged = 0;
+    a.vec_per_row = a.len / 8;
+    a.chunks_per_row = (a.vec_per_row + kThreads * kRowUnroll - 1) / (kThreads * kRowUnroll);
+    a.chunks = a.rows * a.chunks_per_row;
+    a.inv_chunks_per_row = 1.0 / static_cast<double>(a.chunks_per_row);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess ||
+        per_sm <= 0)
+        per_sm = 1;
+    const int64_t grid = std::min<int64_t>(a.chunks, static_cast<int64_t>(sm_count()) * per_sm);
+    kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(a);
+    return check_launch(what);
 }
 
 template <bool HAS_RES, bool SNAKE>
@@ -269,6 +353,13 @@ int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
         a.head = std::min<int64_t>(a.n, static_cast<int64_t>(((32 - phase) % 32) / 4));
         a.nvec = (a.n - a.head) / 8;
         if (a.nvec == 0) vec = false;
+    }
+
+    // Rows form: dense rows of a multiple of 8 values, every tensor 32-byte aligned.
+    if (vec && a.head == 0 && q.len % 8 == 0) {
+        if (q.res)
+            return snake ? launch_rows<true, true>(a, stream, what) : launch_rows<true, false>(a, stream, what);
+        return snake ? launch_rows<false, true>(a, stream, what) : launch_rows<false, false>(a, stream, what);
     }
 
     const int nparams = (snake ? 2 : 0) + (a.has_bias ? 1 : 0);

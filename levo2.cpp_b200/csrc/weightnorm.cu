@@ -1,8 +1,11 @@
 // Weight-norm fold (a9): w[o][:] = v[o][:] * (g[o] / ||v[o][:]||).
 //
-// One CTA per row.  Rows up to 16384 values stay in registers (one HBM read of
-// v, one write of w: 8 B per element); longer rows are streamed twice (the
-// second read mostly hits L2).  The arithmetic follows the reference's numpy
+// One CTA per row, one HBM read of v and one write of w (8 B per element):
+//  * rows up to kMaxStagedCols values are copied into shared memory with
+//    cp.async (a 1024 x 7168 weight: 28 KB per CTA, 7 CTAs per SM, the whole
+//    tensor in flight in one wave), reduced from there and scaled out;
+//  * longer rows up to 16384 values stay in registers, longer still are
+//    streamed twice (the second read mostly hits L2).  The arithmetic follows the reference's numpy
 // expression (convert/convert_vae.py:196-199): norm = sqrt(sum(v*v)) in F32,
 // scale = g / norm, w = v * scale.
 #include <algorithm>
@@ -93,6 +96,39 @@ __global__ void __launch_bounds__(256) weightnorm_vec_kernel(const WnArgs a) {
     }
 }
 
+constexpr int64_t kMaxStagedCols = 12032;  // <= 48 KB of shared memory per CTA with red[]
+
+__global__ void __launch_bounds__(128) weightnorm_staged_kernel(const WnArgs a) {
+    extern __shared__ float4 row_buf[];
+    __shared__ float red[32];
+    const int64_t nchunk = a.cols / 4;
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        const float4 *vr = reinterpret_cast<const float4 *>(a.v + row * a.cols);
+        float4 *wr = reinterpret_cast<float4 *>(a.w + row * a.cols);
+        __syncthreads();  // row_buf is reused across rows
+        for (int64_t i = threadIdx.x; i < nchunk; i += blockDim.x) cp_async16(row_buf + i, vr + i);
+        cp_async_wait_all();
+        __syncthreads();
+        float s = 0.f;
+        for (int64_t i = threadIdx.x; i < nchunk; i += blockDim.x) {
+            const float4 b = row_buf[i];
+            s = fmaf(b.x, b.x, s);
+            s = fmaf(b.y, b.y, s);
+            s = fmaf(b.z, b.z, s);
+            s = fmaf(b.w, b.w, s);
+        }
+        const float scale = row_scale(a, row, block_sum(s, red));
+        for (int64_t i = threadIdx.x; i < nchunk; i += blockDim.x) {
+            float4 b = row_buf[i];
+            b.x = __fmul_rn(b.x, scale);
+            b.y = __fmul_rn(b.y, scale);
+            b.z = __fmul_rn(b.z, scale);
+            b.w = __fmul_rn(b.w, scale);
+            wr[i] = b;
+        }
+    }
+}
+
 // Any row length / alignment.
 __global__ void __launch_bounds__(256) weightnorm_scalar_kernel(const WnArgs a) {
     __shared__ float red[32];
@@ -132,14 +168,21 @@ LEVO_OPS_API int levo_weightnorm_f32(const float *v, const float *g, float *w, f
     const WnArgs a{v, g, w, norms_out, rows, cols};
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const bool vec = cols % 8 == 0 && aligned_to(v, 32) && aligned_to(w, 32);
-    if (!vec) {
+    const bool staged = cols <= kMaxStagedCols && cols % 4 == 0 && aligned_to(v, 16) && aligned_to(w, 16);
+    if (!vec && !staged) {
         const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * 64);
         weightnorm_scalar_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(a);
         return check_launch("levo_weightnorm_f32");
     }
+    if (cols <= kMaxStagedCols && cols % 4 == 0 && aligned_to(v, 16) && aligned_to(w, 16)) {
+        const size_t smem = static_cast<size_t>(cols) * sizeof(float);
+        const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * 16);
+        weightnorm_staged_kernel<<<static_cast<unsigned>(grid), 128, smem, s>>>(a);
+        return check_launch("levo_weightnorm_f32");
+    }
     const int64_t nvec = cols / 8;
-    // 128 threads while the row fits in 8 vectors per thread (single-wave
-    // grids for ~1000-row weights), then 256 threads, then the streamed form.
+    // Register-resident rows: 128 threads while the row fits in 8 vectors per
+    // thread, then 256 threads, then the streamed form.
     const int threads = nvec <= 128 * 8 ? 128 : 256;
     const int64_t vpt = (nvec + threads - 1) / threads;
     switch (vpt) {

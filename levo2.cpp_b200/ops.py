@@ -140,6 +140,8 @@ SIGNATURES = {
     "levo_flow_incontext_f32": (_INT, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "levo_euler_cfg_step_f32": (_INT, [_P, _P, _P, _I64, _I32, _F, _I64, _P, _P]),
     "levo_cfg_euler_multi_f32": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _F, _F, _P, _P]),
+    "levo_gated_layernorm_modulate_f32": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F, _P]),
+    "levo_assemble_windows_f32": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -275,6 +277,21 @@ def add_layernorm_t(x, r, gamma, beta, eps, f16_boundary=False, h_out=None, y_ou
     return h, y
 
 
+def gated_layernorm_modulate_t(x, gate, r, gamma, beta, scale, shift, batch_rows, eps=1e-5, h_out=None,
+                               y_out=None):
+    """Flow block tail: h = r + x*gate[b]; y = (LN(h)*gamma + beta)*(1 + scale[b]) + shift[b]."""
+    import torch
+
+    _require_cuda(x, gate, r, gamma, beta, scale, shift, h_out, y_out)
+    h = torch.empty_like(x) if h_out is None else h_out
+    y = torch.empty_like(x) if y_out is None else y_out
+    rows, dim = x.shape
+    check(lib().levo_gated_layernorm_modulate_f32(_ptr(x), _ptr(gate), _ptr(r), _ptr(gamma), _ptr(beta), _ptr(scale),
+                                                  _ptr(shift), batch_rows, _ptr(h), _ptr(y), rows, dim, eps,
+                                                  _stream(x.device)))
+    return h, y
+
+
 def weightnorm_t(v, g, w=None, norms=None):
     """w = v * (g / ||v||) per dim-0 row; v is [rows, ...] F32, g has one value per row."""
     import torch
@@ -330,6 +347,21 @@ def cfg_euler_multi_t(state, noise, context, uncond, cond, *, batch, prefix, fir
     check(lib().levo_cfg_euler_multi_f32(_ptr(state), _ptr(noise), _ptr(context), _ptr(uncond), _ptr(cond),
                                          batch, row, prefix, first_step, count, steps, 1 if cfg else 0, guidance,
                                          sigma_min, _ptr(status), _stream(state.device)))
+
+
+def assemble_windows_t(windows, hop_samples: int, overlap_samples: int, target_samples: int, interleaved=False,
+                       out=None):
+    """Crossfade-assemble decoded windows [W, C, S] into [C, target] (or [target, C] interleaved)."""
+    import torch
+
+    _require_cuda(windows, out)
+    w, c, s = windows.shape
+    if out is None:
+        shape = (target_samples, c) if interleaved else (c, target_samples)
+        out = torch.empty(shape, dtype=torch.float32, device=windows.device)
+    check(lib().levo_assemble_windows_f32(_ptr(windows), w, c, s, hop_samples, overlap_samples, target_samples,
+                                          _ptr(out), 1 if interleaved else 0, _stream(windows.device)))
+    return out
 
 
 def reference_topology() -> Topology:

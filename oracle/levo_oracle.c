@@ -416,6 +416,39 @@ int oracle_add_layernorm_f32(const float *x, const float *r, const float *gamma,
     return run_norm(x, r, gamma, beta, h_out, y_out, rows, dim, eps, 0, 1, 0, threads);
 }
 
+int oracle_gated_layernorm_modulate_f32(const float *x, const float *gate, const float *r,
+                                        const float *gamma, const float *beta, const float *scale,
+                                        const float *shift, int64_t batch_rows, float *h_out,
+                                        float *y_out, int64_t rows, int64_t dim, float eps) {
+    if (!x || !gamma || !beta || !y_out || rows < 0 || dim <= 0 || batch_rows <= 0) return -1;
+    float *h = (float *)malloc(sizeof(float) * (size_t)(rows * dim));
+    if (!h) return -2;
+    for (int64_t row = 0; row < rows; ++row) {
+        const int64_t b = (row / batch_rows) * dim;
+        for (int64_t i = 0; i < dim; ++i) {
+            const int64_t e = row * dim + i;
+            float v = x[e];
+            if (gate) v = v * gate[b + i];      /* ggml_mul(branch, gate chunk) */
+            if (r) v = v + r[e];                /* ggml_add(., residual) */
+            h[e] = v;
+        }
+    }
+    if (h_out) memcpy(h_out, h, sizeof(float) * (size_t)(rows * dim));
+    run_norm(h, NULL, gamma, beta, NULL, y_out, rows, dim, eps, 0, 1, 0, 1);
+    for (int64_t row = 0; row < rows; ++row) {
+        const int64_t b = (row / batch_rows) * dim;
+        for (int64_t i = 0; i < dim; ++i) {
+            const int64_t e = row * dim + i;
+            float y = y_out[e];
+            if (scale) y = y * (scale[b + i] * 1.0f + 1.0f); /* add_scale_shift: mul by 1+scale */
+            if (shift) y = y + shift[b + i];                  /* then add shift */
+            y_out[e] = y;
+        }
+    }
+    free(h);
+    return 0;
+}
+
 /* ------------------------------------------------------------------------ */
 /* weight norm                                                               */
 /* ------------------------------------------------------------------------ */
@@ -500,5 +533,39 @@ int oracle_cfg_euler_f32(float *state, const float *noise, const float *context,
         for (int64_t b = 0; b < batch; ++b)
             memcpy(state + b * row, context + b * row, sizeof(float) * (size_t)prefix);
     free(v);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* window assembly                                                           */
+/* ------------------------------------------------------------------------ */
+
+int oracle_assemble_windows_f32(const float *windows, int64_t n, int64_t channels,
+                                int64_t window_samples, int64_t hop, int64_t overlap,
+                                int64_t target, float *out) {
+    if (!windows || !out || n <= 0 || channels <= 0 || window_samples <= 0 || hop <= 0) return -1;
+    const int64_t assembled = (n - 1) * hop + window_samples;
+    if (target > assembled) return -1;
+    float *full = (float *)calloc((size_t)(channels * assembled), sizeof(float));
+    if (!full) return -2;
+    for (int64_t c = 0; c < channels; ++c) {
+        float *o = full + c * assembled;
+        for (int64_t k = 0; k < n; ++k) {
+            const float *d = windows + (k * channels + c) * window_samples;
+            const int64_t offset = k * hop;
+            if (k == 0) { /* :167-171 */
+                memcpy(o + offset, d, sizeof(float) * (size_t)window_samples);
+                continue;
+            }
+            const float denominator = (float)(overlap - 1); /* :184-191 */
+            for (int64_t s = 0; s < overlap; ++s) {
+                const float alpha = (float)s / denominator;
+                o[offset + s] = o[offset + s] * (1.0f - alpha) + d[s] * alpha;
+            }
+            memcpy(o + offset + overlap, d + overlap, sizeof(float) * (size_t)(window_samples - overlap));
+        }
+        memcpy(out + c * target, o, sizeof(float) * (size_t)target); /* :198-201 crop */
+    }
+    free(full);
     return 0;
 }

@@ -67,6 +67,14 @@ int oracle_add_layernorm_f32(const float *x, const float *r, const float *gamma,
                              float *h_out, float *y_out, int64_t rows, int64_t dim, float eps,
                              int threads);
 
+/* Flow block tail, node by node (src/levo-flow-estimator.cpp:89-93,106-109,221-227):
+ * h = x*gate[b] + r; y = ((norm(h)*gamma + beta) * (scale[b]*1 + 1)) + shift[b],
+ * b = row / batch_rows; gate / r / scale / shift may be NULL. */
+int oracle_gated_layernorm_modulate_f32(const float *x, const float *gate, const float *r,
+                                        const float *gamma, const float *beta, const float *scale,
+                                        const float *shift, int64_t batch_rows, float *h_out,
+                                        float *y_out, int64_t rows, int64_t dim, float eps);
+
 /* Weight-norm fold, convert/convert_vae.py:196-199.  norms_out may be NULL.
  * Returns -1 (and still writes w) when a row norm is zero, as the reference
  * raises ValueError. */
@@ -81,12 +89,19 @@ int oracle_cfg_combine_f32(const float *uncond, const float *cond, float *out, i
  * solve_flow_euler (src/levo-flow-renderer.cpp:57-120) for each of `batch`
  * independent rows: runs steps [first_step, first_step + count) and restores
  * the context prefix when the last step has run.  Returns -1 on a non-finite
- * velocity or state (the reference throws), leaving `state` at the last
- * completed step. */
+ * velocity or state (the reference throws); `state` is then unspecified, as the
+ * reference discards its local state and keeps only the last checkpoint. */
 int oracle_cfg_euler_f32(float *state, const float *noise, const float *context,
                          const float *uncond, const float *cond, int64_t batch, int64_t row,
                          int64_t prefix, int64_t first_step, int64_t count, int64_t steps, int cfg,
                          float guidance, float sigma_min);
+
+/* Window crossfade assembly, src/levo-renderer-pattern.cpp:137-203, over
+ * windows [n][channels][window_samples] -> planar [channels][target]; the
+ * reference's sequential copy-then-crossfade loop. */
+int oracle_assemble_windows_f32(const float *windows, int64_t n, int64_t channels,
+                                int64_t window_samples, int64_t hop, int64_t overlap,
+                                int64_t target, float *out);
 
 /* IEEE half <-> float (round to nearest even). */
 float oracle_half_to_float(uint16_t h);

@@ -36,6 +36,8 @@ _SIGS = {
     "oracle_add_layernorm_f32": [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _INT],
     "oracle_weightnorm_f32": [_P, _P, _P, _P, _I64, _I64, _INT],
     "oracle_cfg_combine_f32": [_P, _P, _P, _I64, _F],
+    "oracle_gated_layernorm_modulate_f32": [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F],
+    "oracle_assemble_windows_f32": [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P],
     "oracle_cfg_euler_f32": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _F, _F],
 }
 
@@ -184,6 +186,18 @@ def add_layernorm(x, r, gamma, beta, eps, f16_boundary=False, threads: int = 0):
     return _norm(True, x, r, gamma, beta, eps, f16_boundary, threads)
 
 
+def gated_layernorm_modulate(x, gate, r, gamma, beta, scale, shift, batch_rows, eps=1e-5):
+    x = _f32(x)
+    f = lambda a: None if a is None else _f32(a)  # noqa: E731
+    gate, r, gamma, beta, scale, shift = map(f, (gate, r, gamma, beta, scale, shift))
+    h = np.empty_like(x)
+    y = np.empty_like(x)
+    rc = lib().oracle_gated_layernorm_modulate_f32(_p(x), _p(gate), _p(r), _p(gamma), _p(beta), _p(scale), _p(shift),
+                                                   batch_rows, _p(h), _p(y), x.shape[0], x.shape[1], eps)
+    assert rc == 0
+    return h, y
+
+
 def weightnorm(v, g, threads: int = 0):
     """Returns (w, norms, ok) where ok is False when a row norm is zero."""
     v = _f32(v)
@@ -217,6 +231,14 @@ def cfg_euler(state, noise, context, uncond, cond, *, batch, prefix, first_step,
                                     count, steps, 1 if cfg else 0, guidance, sigma_min)
     assert rc in (0, -1)
     return st, rc == 0
+
+
+def assemble_windows(windows, hop, overlap, target) -> np.ndarray:
+    w = _f32(windows)
+    n, c, s = w.shape
+    out = np.empty((c, target), np.float32)
+    assert lib().oracle_assemble_windows_f32(_p(w), n, c, s, hop, overlap, target, _p(out)) == 0
+    return out
 
 
 # --------------------------------------------------------------------------- reference (compiled sources)

@@ -143,3 +143,33 @@ def test_weightnorm_zero_norm_raises_like_the_reference(ops, dev):
     v[2] = 0
     with pytest.raises(ValueError, match="zero weight-norm"):
         ops.fold_weight_norm_t(v, torch.ones(3, device=dev))
+
+
+# --------------------------------------------------------------------------- Flow block tail (next item)
+
+@pytest.mark.parametrize("dim", [2200, 64, 13])
+@pytest.mark.parametrize("parts", ["all", "no_gate", "no_residual", "no_mod"])
+def test_gated_layernorm_modulate_matches_oracle(ops, orc, dev, dim, parts):
+    # Flow estimator block: [batch=2, frames, 2200] F32 (src/levo-flow-estimator.cpp:89-93,106-109,221-227)
+    rng = np.random.default_rng(dim + len(parts))
+    batch, frames = 2, 50
+    rows = batch * frames
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    r = None if parts == "no_residual" else rng.standard_normal((rows, dim)).astype(np.float32)
+    gate = None if parts == "no_gate" else rng.standard_normal((batch, dim)).astype(np.float32)
+    gamma = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    beta = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+    scale = None if parts == "no_mod" else (0.1 * rng.standard_normal((batch, dim))).astype(np.float32)
+    shift = None if parts == "no_mod" else (0.1 * rng.standard_normal((batch, dim))).astype(np.float32)
+    T = lambda a: None if a is None else torch.from_numpy(a).to(dev)  # noqa: E731
+    h, y = ops.gated_layernorm_modulate_t(T(x), T(gate), T(r), T(gamma), T(beta), T(scale), T(shift), frames)
+    hw, yw = orc.gated_layernorm_modulate(x, gate, r, gamma, beta, scale, shift, frames)
+    assert np.array_equal(h.cpu().numpy(), hw)  # products and sums only: bit-exact
+    assert_close(y.cpu().numpy(), yw, 1e-5, parts)
+
+
+def test_gated_layernorm_modulate_rejects_bad_batch(ops, dev):
+    x = torch.zeros((10, 64), device=dev)
+    g = torch.ones(64, device=dev)
+    with pytest.raises(ValueError, match="batch_rows"):
+        ops.gated_layernorm_modulate_t(x, None, None, g, g, None, None, 3)

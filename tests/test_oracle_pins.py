@@ -244,3 +244,51 @@ def test_chain_oracle_stage_shapes_and_determinism(orc, ops):
     a1 = orc.vae_chain(t.as_list(), p, lat, 5, 2, 30, threads=1)
     a2 = orc.vae_chain(t.as_list(), p, lat, 5, 2, 30, threads=4)
     assert a1.shape == (2, 30) and np.all(np.isfinite(a1)) and np.array_equal(a1, a2)
+
+
+# --------------------------------------------------------------------------- window assembly (next item)
+
+def test_assembly_known_answer(orc):
+    # tests/test-renderer-pattern.cpp:93-108: two windows of constant 1/3 (left) and 2/4 (right)
+    win, hop, ov = 1000 * 1920, 750 * 1920, 250 * 1920
+    target = 1001 * 1920
+    w = np.empty((2, 2, win), np.float32)
+    w[0, 0], w[0, 1], w[1, 0], w[1, 1] = 1.0, 2.0, 3.0, 4.0
+    out = orc.assemble_windows(w, hop, ov, target)
+    assert out.shape == (2, target)
+    assert abs(out[0, hop] - 1.0) < 1e-6 and abs(out[0, hop + ov - 1] - 3.0) < 1e-6
+    assert abs(out[0, hop + ov] - 3.0) < 1e-6
+    assert abs(out[1, 0] - 2.0) < 1e-6 and abs(out[1, -1] - 4.0) < 1e-6
+
+
+@needs_ref
+@pytest.mark.parametrize("source_frames", [1001, 1751])
+def test_assembly_oracle_bit_exact_vs_reference_code(source_frames):
+    import __graft_entry__ as entry
+
+    orc = entry.load_oracle()
+    sched = orc.ref_make_renderer_schedule(source_frames)
+    n = len(sched["windows"])
+    win = int(sched["windows"][0][2])
+    rng = np.random.default_rng(source_frames)
+    w = rng.standard_normal((n, 2, win)).astype(np.float32)
+    ref_l, ref_r = orc.ref_assemble_renderer_audio(source_frames, w[:, 0], w[:, 1])
+    got = orc.assemble_windows(w, 750 * 1920, 250 * 1920, sched["target_samples"])
+    assert np.array_equal(got[0], ref_l) and np.array_equal(got[1], ref_r)
+
+
+def test_gated_layernorm_modulate_matches_definition(orc):
+    rng = np.random.default_rng(9)
+    batch, frames, dim = 2, 7, 300
+    x, r = rng.standard_normal((2, batch * frames, dim)).astype(np.float32)
+    gate, scale, shift = rng.standard_normal((3, batch, dim)).astype(np.float32)
+    gamma = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    beta = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+    h, y = orc.gated_layernorm_modulate(x, gate, r, gamma, beta, scale, shift, frames)
+    b = np.repeat(np.arange(batch), frames)
+    hh = x.astype(np.float64) * gate[b] + r
+    mu = hh.mean(1, keepdims=True)
+    n = (hh - mu) / np.sqrt(((hh - mu) ** 2).mean(1, keepdims=True) + 1e-5)
+    want = (n * gamma + beta) * (1 + scale[b]) + shift[b]
+    assert_close(h, hh, 1e-6)
+    assert_close(y, want, 1e-5)
