@@ -1,12 +1,17 @@
 // Residual add + RMSNorm / LayerNorm row reductions (a5, a6).
 //
-// Vector path: a row group of 32*wpr threads owns one row; the row stays in
-// registers (<= 64 F32 values per thread), so x and r are read from HBM once
-// and h and y written once: 8 B per element for F16 activations.  Row sums are
-// reduced with warp shuffles (and shared memory across the warps of a group
-// when wpr > 1).  LayerNorm is two-pass over the register-resident row.
-// Scalar path (rows whose byte length is not a multiple of 32, or unaligned
-// pointers): one CTA per row, re-reading the row from L2.
+// Every form reads x and r from HBM once and writes h and y once: 8 B per
+// element for F16 activations.
+// Staged path (the common case: rows of <= 12.5 KB, 16-byte aligned): one warp
+// per row, 8 rows per CTA.  x and r are copied into shared memory with cp.async
+// so the whole input is in flight at once without holding it in registers
+// (4096 x 1536 F16: 48 KB per CTA, 4 CTAs per SM, one wave); h = x + r is
+// written back over x, the row statistics are reduced with warp shuffles
+// (LayerNorm two-pass over shared memory), and y leaves in 16-byte stores.
+// Vector path (longer rows): a row group of 32*wpr threads keeps the row in
+// registers (<= 64 F32 values per thread) and reduces across warps in shared
+// memory.  Scalar path (rows whose byte length is not a multiple of 16, or
+// unaligned pointers): one CTA per row, re-reading the row from L2.
 #include <algorithm>
 #include <cmath>
 
@@ -286,6 +291,157 @@ __global__ void __launch_bounds__(kThreads, (!LAYER && !MOD && VPL * Act<T>::kVe
     }
 }
 
+constexpr int kStagedRows = 8;                   // warps = rows per CTA
+constexpr size_t kStagedMaxSmem = 200 * 1024;    // opt-in dynamic shared memory cap
+
+template <typename T>
+struct Chunk;  // 16 bytes of activations
+template <>
+struct Chunk<__half> {
+    static constexpr int kN = 8;
+    __device__ static void unpack(const uint4 &c, float *v) {
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+    __device__ static uint4 pack(const float *v) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t *>(&h2);
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+};
+template <>
+struct Chunk<float> {
+    static constexpr int kN = 4;
+    __device__ static void unpack(const uint4 &c, float *v) {
+        v[0] = __uint_as_float(c.x);
+        v[1] = __uint_as_float(c.y);
+        v[2] = __uint_as_float(c.z);
+        v[3] = __uint_as_float(c.w);
+    }
+    __device__ static uint4 pack(const float *v) {
+        return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                          __float_as_uint(v[3]));
+    }
+};
+
+// kN consecutive F32 column parameters starting at p (16-byte aligned).
+template <int N>
+__device__ __forceinline__ void load_cols(const float *p, float *out) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+        const float4 f = __ldg(reinterpret_cast<const float4 *>(p + i));
+        out[i] = f.x;
+        out[i + 1] = f.y;
+        out[i + 2] = f.z;
+        out[i + 3] = f.w;
+    }
+}
+
+template <typename T, bool LAYER, bool MOD>
+__global__ void __launch_bounds__(kStagedRows * 32) add_norm_staged_kernel(const NormArgs a) {
+    extern __shared__ uint4 sbuf[];
+    constexpr int N = Chunk<T>::kN;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int chunks = a.dim / N;
+    uint4 *xs = sbuf + static_cast<size_t>(warp) * 2 * chunks;
+    uint4 *rs = xs + chunks;
+    const float inv_dim = 1.0f / static_cast<float>(a.dim);
+    for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * kStagedRows; row0 < a.rows;
+         row0 += static_cast<int64_t>(gridDim.x) * kStagedRows) {
+        const int64_t row = row0 + warp;
+        if (row >= a.rows) continue;  // warp-uniform; no CTA-wide barrier in this loop
+        const uint4 *xg = reinterpret_cast<const uint4 *>(static_cast<const char *>(a.x) + row * a.dim * sizeof(T));
+        const uint4 *rg = a.r ? reinterpret_cast<const uint4 *>(static_cast<const char *>(a.r) + row * a.dim * sizeof(T))
+                              : nullptr;
+        const int64_t mod_off = MOD ? (row / a.batch_rows) * a.dim : 0;
+        __syncwarp();  // the previous row's shared-memory reads are done
+        for (int i = lane; i < chunks; i += 32) {
+            cp_async16(xs + i, xg + i);
+            if (rg) cp_async16(rs + i, rg + i);
+        }
+        cp_async_wait_all();
+        __syncwarp();
+        // pass 1: h = [x * gate] + r (rounded to T) back into xs; row sum / sum of squares
+        float sum = 0.f;
+        for (int i = lane; i < chunks; i += 32) {
+            float h[N];
+            Chunk<T>::unpack(xs[i], h);
+            const bool gated = MOD && a.gate;
+            if (gated) {
+                float g[N];
+                load_cols<N>(a.gate + mod_off + i * N, g);
+#pragma unroll
+                for (int j = 0; j < N; ++j) h[j] = __fmul_rn(h[j], g[j]);
+            }
+            if (rg) {
+                float r[N];
+                Chunk<T>::unpack(rs[i], r);
+#pragma unroll
+                for (int j = 0; j < N; ++j) h[j] = __fadd_rn(h[j], r[j]);
+            }
+            if (gated || rg) {
+#pragma unroll
+                for (int j = 0; j < N; ++j) h[j] = Act<T>::round(h[j]);
+                xs[i] = Chunk<T>::pack(h);
+            }
+#pragma unroll
+            for (int j = 0; j < N; ++j) sum += LAYER ? h[j] : h[j] * h[j];
+        }
+        sum = warp_sum(sum);
+        float mean = 0.f, scale;
+        if (LAYER) {
+            mean = sum * inv_dim;
+            float sq = 0.f;
+            for (int i = lane; i < chunks; i += 32) {
+                float h[N];
+                Chunk<T>::unpack(xs[i], h);
+#pragma unroll
+                for (int j = 0; j < N; ++j) {
+                    const float d = __fsub_rn(h[j], mean);
+                    sq += d * d;
+                }
+            }
+            sq = warp_sum(sq);
+            scale = 1.0f / sqrtf(sq * inv_dim + a.eps);
+        } else {
+            scale = 1.0f / sqrtf(sum * inv_dim + a.eps);
+        }
+        uint4 *hg = (a.h_out && (rg || (MOD && a.gate)))
+                        ? reinterpret_cast<uint4 *>(static_cast<char *>(a.h_out) + row * a.dim * sizeof(T))
+                        : nullptr;
+        uint4 *yg = reinterpret_cast<uint4 *>(static_cast<char *>(a.y_out) + row * a.dim * sizeof(T));
+        for (int i = lane; i < chunks; i += 32) {
+            const uint4 hc = xs[i];
+            if (hg) hg[i] = hc;
+            float h[N], g[N], b[N];
+            Chunk<T>::unpack(hc, h);
+            load_cols<N>(a.gamma + i * N, g);
+            if (LAYER) load_cols<N>(a.beta + i * N, b);
+            float ms[N], mh[N];
+            if (MOD && a.scale) load_cols<N>(a.scale + mod_off + i * N, ms);
+            if (MOD && a.shift) load_cols<N>(a.shift + mod_off + i * N, mh);
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                const float n = LAYER ? __fmul_rn(__fsub_rn(h[j], mean), scale) : __fmul_rn(h[j], scale);
+                float y = norm_output<T, LAYER>(a, n, g[j], LAYER ? b[j] : 0.f);
+                if (MOD) y = modulate(a, y, (a.scale ? ms[j] : 0.f), (a.shift ? mh[j] : 0.f));
+                h[j] = y;
+            }
+            yg[i] = Chunk<T>::pack(h);
+        }
+    }
+}
+
 // Fallback: one CTA per row, any dim and alignment.
 template <typename T, bool LAYER>
 __global__ void __launch_bounds__(kThreads) add_norm_scalar_kernel(const NormArgs a) {
@@ -383,6 +539,32 @@ int run_norm(const char *what, const void *x, const void *r, const float *gamma,
             return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
     NormArgs a{x, r, gamma, beta, h_out, y_out, rows, static_cast<int>(dim), 1, eps,
                (flags & LEVO_NORM_F16_BOUNDARY) ? 1 : 0, gate, mscale, mshift, MOD ? batch_rows : 0};
+    {
+        const size_t smem = static_cast<size_t>(kStagedRows) * 2 * dim * sizeof(T);
+        bool staged = (dim * sizeof(T)) % 16 == 0 && dim % 4 == 0 && smem <= kStagedMaxSmem;
+        for (int i = 0; i < 6 && staged; ++i)
+            if (ptrs[i] && !aligned_to(ptrs[i], 16)) staged = false;
+        for (const void *m : mods)
+            if (m && !aligned_to(m, 16)) staged = false;
+        if (staged) {
+            auto kernel = add_norm_staged_kernel<T, LAYER, MOD>;
+            if (smem > 48 * 1024 &&
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)) != cudaSuccess)
+                staged = false;
+            if (staged) {
+                int per_sm = 0;
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kStagedRows * 32, smem) !=
+                        cudaSuccess ||
+                    per_sm <= 0)
+                    per_sm = 1;
+                const int64_t grid = std::min<int64_t>((rows + kStagedRows - 1) / kStagedRows,
+                                                       static_cast<int64_t>(sm_count()) * per_sm);
+                kernel<<<static_cast<unsigned>(grid), kStagedRows * 32, smem, stream>>>(a);
+                return check_launch(what);
+            }
+        }
+    }
     constexpr int VE = Act<T>::kVec;
     constexpr int kMaxVpl = sizeof(T) == 2 ? 4 : 8;  // <= 64 F32 values per thread
     bool vec = (dim * sizeof(T)) % 32 == 0 && (dim % 8 == 0);
