@@ -107,8 +107,7 @@ __device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelPar
 // Rows form: CTA b owns chunks [b*chunks/G, (b+1)*chunks/G); chunk q covers
 // vectors [k*kThreads*UNROLL, (k+1)*kThreads*UNROLL) of row c, q = c*cpr + k.
 template <bool HAS_RES, bool SNAKE, int UNROLL>
-// 64 registers: 4 CTAs (32 warps) per SM keep more 256-bit loads in flight.
-__global__ void __launch_bounds__(kThreads, 4) stream_rows_kernel(const StreamArgs a) {
+__global__ void __launch_bounds__(kThreads) stream_rows_kernel(const StreamArgs a) {
     const int64_t q0 = a.chunks * blockIdx.x / gridDim.x;
     const int64_t q1 = a.chunks * (blockIdx.x + 1) / gridDim.x;
     if (q0 >= q1) return;
