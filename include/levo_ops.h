@@ -248,6 +248,34 @@ typedef struct {
  * since the last reset (out has LEVO_KCLASS_COUNT entries). */
 LEVO_OPS_API int levo_vae_chain_timing(levo_vae_chain *chain, levo_kernel_timing *out, int reset);
 
+/*
+ * Allocation-free decode of one window.  This entry point has no counterpart in
+ * the reference: it exists for callers that cannot let a library call
+ * cudaMalloc, such as a real-time render thread (an allocation can synchronise
+ * the whole device) or a host engine that owns a fixed device-memory budget and
+ * hands out only its own buffers.
+ *
+ * Same work and result as levo_vae_chain_decode, but without a levo_vae_chain:
+ *   params  device pointer to the packed parameters (levo_vae_param_count floats),
+ *   latent  device [latent_dim][frames], audio device [audio_channels][frames * prod(strides)],
+ *   conv    optional convolution callback (NULL: built-in stand-ins), as for the chain.
+ * The three activation buffers come from one static device array of
+ * 3 x 2^21 floats (24 MiB) that every GPU loading this library holds until the
+ * process exits; the largest activation tensor of the window must fit in
+ * 2^21 floats (the reference topology: frames <= 8), else LEVO_OPS_EINVAL.
+ * Nothing is allocated: no cudaMalloc, no cudaFree, no events.
+ * The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture.  All calls on a device share the array and it keeps the
+ * previous call's contents (the decode writes every value before reading it,
+ * so nothing needs clearing); calls that overlap on the GPU (other streams,
+ * other threads) race on it.  flags: LEVO_CHAIN_TANH only.
+ */
+LEVO_OPS_API int levo_vae_decode_noalloc_f32(const levo_vae_topology *topology, const float *params,
+                                             const float *latent, int64_t frames, float *audio,
+                                             levo_conv_fn conv, void *conv_user, uint32_t flags,
+                                             levo_stream_t stream);
+
 /* Built-in conv stand-in: out[c][t] = in[c mod in_channels][t / stride]. */
 LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int64_t in_length,
                                        float *out, int64_t out_channels, int64_t out_length,

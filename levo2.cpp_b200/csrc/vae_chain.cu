@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -722,6 +723,113 @@ LEVO_OPS_API int levo_vae_chain_timing(levo_vae_chain *chain, levo_kernel_timing
     std::memcpy(out, chain->totals, sizeof(chain->totals));
     if (reset) std::memset(chain->totals, 0, sizeof(chain->totals));
     return LEVO_OPS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode (levo_vae_decode_noalloc_f32)
+//
+// Some callers cannot let this library call cudaMalloc: a real-time render
+// thread (cudaMalloc may synchronise the whole device), or a host engine that
+// owns a fixed device-memory budget and hands out only its own buffers (as the
+// reference's GGML backend does with its graph allocator).  For them the three
+// activation buffers of the decoder chain live in one file-scope device array
+// of fixed size instead of a levo_vae_chain workspace.  Every GPU that loads
+// this library holds the array (kNoallocFloats floats, 24 MiB) until the
+// process exits.
+// ---------------------------------------------------------------------------
+namespace levo {
+namespace {
+
+constexpr int64_t kNoallocBufferFloats = int64_t(1) << 21;           // one activation buffer: 8 MiB
+constexpr int64_t kNoallocFloats = 3 * kNoallocBufferFloats;          // X, A and B: 24 MiB
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoallocFloats];
+
+// Device address of g_noalloc_scratch per device, resolved once with that
+// device current (the symbol's host-side name is not a device address).
+constexpr int kNoallocMaxDevices = 64;
+float *g_noalloc_ptr[kNoallocMaxDevices] = {};
+std::mutex g_noalloc_mutex;
+
+int noalloc_scratch(int device, float **out) {
+    if (device < 0 || device >= kNoallocMaxDevices)
+        return set_error(LEVO_OPS_EUNSUPPORTED, "levo_vae_decode_noalloc_f32: device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[device] == nullptr) {
+        void *ptr = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (err != cudaSuccess || ptr == nullptr)
+            return set_error(LEVO_OPS_ECUDA, std::string("levo_vae_decode_noalloc_f32: cannot resolve the "
+                                                         "static scratch array: ") + cudaGetErrorString(err));
+        g_noalloc_ptr[device] = static_cast<float *>(ptr);
+    }
+    *out = g_noalloc_ptr[device];
+    return LEVO_OPS_OK;
+}
+
+}  // namespace
+}  // namespace levo
+
+extern "C" {
+
+LEVO_OPS_API int levo_vae_decode_noalloc_f32(const levo_vae_topology *topology, const float *params,
+                                             const float *latent, int64_t frames, float *audio,
+                                             levo_conv_fn conv, void *conv_user, uint32_t flags,
+                                             levo_stream_t stream) {
+    using namespace levo;
+    clear_error();
+    const char *w = "levo_vae_decode_noalloc_f32";
+    std::string why;
+    if (topology == nullptr || !valid_topology(*topology, &why))
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": invalid topology: " + why);
+    if (params == nullptr || latent == nullptr || audio == nullptr)
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": required pointer is null");
+    if (!aligned_to(params, 4) || !aligned_to(latent, 4) || !aligned_to(audio, 4))
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": pointer is not 4-byte aligned");
+    if (flags & ~LEVO_CHAIN_TANH)
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": only LEVO_CHAIN_TANH is accepted");
+    if (frames <= 0) return set_error(LEVO_OPS_EINVAL, std::string(w) + ": latent frame count must be positive");
+    // Largest activation tensor of the stage loop; each of the three buffers must hold it.
+    int64_t elems = static_cast<int64_t>(topology->entry_width) * frames;
+    int64_t len = frames;
+    int64_t cin = topology->entry_width;
+    for (int st = 0; st < topology->n_stages; ++st) {
+        if (len > kNoallocBufferFloats) break;
+        elems = std::max(elems, cin * len);
+        len *= topology->stage_stride[st];
+        elems = std::max(elems, static_cast<int64_t>(topology->stage_width[st]) * len);
+        cin = topology->stage_width[st];
+    }
+    if (elems > kNoallocBufferFloats || len > kNoallocBufferFloats)
+        return set_error(LEVO_OPS_EINVAL,
+                         std::string(w) + ": the largest activation tensor (" + std::to_string(elems) +
+                             " floats) exceeds the static scratch limit of " +
+                             std::to_string(kNoallocBufferFloats) +
+                             " floats per buffer; use levo_vae_chain_create / levo_vae_chain_decode");
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess)
+        return set_error(LEVO_OPS_ECUDA, std::string(w) + ": no current CUDA device");
+    float *scratch = nullptr;
+    const int rc = noalloc_scratch(device, &scratch);
+    if (rc != LEVO_OPS_OK) return rc;
+
+    // A chain view over caller memory and the static scratch: no workspace,
+    // no events, nothing allocated.
+    levo_vae_chain view;
+    view.device = device;
+    view.topo = *topology;
+    view.layout = make_layout(*topology);
+    view.max_frames = frames;
+    view.max_elems = kNoallocBufferFloats;
+    view.params = const_cast<float *>(params);
+    view.X = scratch;
+    view.A = scratch + kNoallocBufferFloats;
+    view.B = scratch + 2 * kNoallocBufferFloats;
+    view.conv = conv;
+    view.conv_user = conv_user;
+    return decode_one(&view, latent, frames, audio, flags, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

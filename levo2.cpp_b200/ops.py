@@ -141,6 +141,7 @@ SIGNATURES = {
     "levo_euler_cfg_step_f32": (_INT, [_P, _P, _P, _I64, _I32, _F, _I64, _P, _P]),
     "levo_cfg_euler_multi_f32": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _F, _F, _P, _P]),
     "levo_gated_layernorm_modulate_f32": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F, _P]),
+    "levo_vae_decode_noalloc_f32": (_INT, [ctypes.POINTER(Topology), _P, _P, _I64, _P, CONV_FN, _P, _U32, _P]),
     "levo_assemble_windows_f32": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P]),
 }
 
