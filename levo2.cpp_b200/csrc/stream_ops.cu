@@ -362,8 +362,12 @@ int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
         return snake ? launch_rows<false, true>(a, stream, what) : launch_rows<false, false>(a, stream, what);
     }
 
+    // Stage the per-channel parameters in shared memory only when each CTA has
+    // enough elements to amortise exponentiating all of them (the stage-0 entry
+    // unit, 2048 channels x 750 frames, computes them per vector instead).
     const int nparams = (snake ? 2 : 0) + (a.has_bias ? 1 : 0);
-    a.staged = nparams > 0 && q.rows <= kMaxStagedChannels;
+    const int64_t per_cta = a.n / (static_cast<int64_t>(sm_count()) * 8);
+    a.staged = nparams > 0 && q.rows <= kMaxStagedChannels && q.rows * 64 <= per_cta;
     const size_t smem_bytes = a.staged ? static_cast<size_t>(3 * q.rows) * sizeof(float) : 0;
 
     if (q.res) {

@@ -31,17 +31,27 @@ int fused_unit(const levo_fused_unit &unit, cudaStream_t stream);
 
 namespace {
 
+// Row form for any row length: blockIdx.y walks output rows, each thread writes
+// 4 consecutive samples of the row (one division by the stride per 4 samples).
 __global__ void __launch_bounds__(256) conv_standin_kernel(const float *in, int64_t cin, int64_t lin,
                                                           float *out, int64_t cout, int64_t lout,
                                                           int32_t stride) {
-    const int64_t n = cout * lout;
-    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n;
-         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t c = e / lout;
-        const int64_t t = e - c * lout;
-        const int64_t sc = c % cin;
-        const int64_t st = t / stride;
-        out[e] = st < lin ? in[sc * lin + st] : 0.f;
+    for (int64_t c = blockIdx.y; c < cout; c += gridDim.y) {
+        const float *src = in + (c % cin) * lin;
+        float *dst = out + c * lout;
+        for (int64_t t0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; t0 < lout;
+             t0 += static_cast<int64_t>(gridDim.x) * blockDim.x * 4) {
+            int64_t st = t0 / stride;
+            int32_t phase = static_cast<int32_t>(t0 - st * stride);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (t0 + k < lout) dst[t0 + k] = st < lin ? __ldg(src + st) : 0.f;
+                if (++phase == stride) {
+                    phase = 0;
+                    ++st;
+                }
+            }
+        }
     }
 }
 
@@ -551,9 +561,10 @@ LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int
             in, in_channels, in_length, out, out_channels, out_length, stride,
             1.0 / static_cast<double>(out_length));
     } else {
-        const int64_t grid = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
-        conv_standin_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(in, in_channels, in_length, out,
-                                                                     out_channels, out_length, stride);
+        const int64_t gx = std::min<int64_t>((out_length + 1023) / 1024, 64);
+        const int64_t gy = std::min<int64_t>(out_channels, 65535);
+        conv_standin_kernel<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), 256, 0, s>>>(
+            in, in_channels, in_length, out, out_channels, out_length, stride);
     }
     return check_launch("levo_conv_standin_f32");
 }
