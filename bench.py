@@ -46,6 +46,12 @@ SEED = 1234
 FRAME_RATE = 25.0  # latent frames per audio second (src/levo-renderer-pattern.h:221)
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "vae_decode_audio_sec_per_sec"
+_JSON_OUT = sys.stdout
+
+
+def emit(line: dict) -> None:
+    _JSON_OUT.write(json.dumps(line) + "\n")
+    _JSON_OUT.flush()
 
 
 def parse():
@@ -280,7 +286,7 @@ def reference_arm(args):
         "note": ("the reference's GGML CPU backend is not buildable here (ggml submodule absent); this is its "
                  "node-by-node CPU restatement in oracle/, one materialised pass per GGML node"),
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -512,7 +518,7 @@ def own_arm(args):
     chain.close()
     d.close()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
     return 0
 
 
@@ -523,11 +529,17 @@ def only_kernels(args):
     torch.cuda.set_device(dev)
     ops = entry.load_package().ops
     peak, _ = measured_peak()
-    print(json.dumps({"kernels": kernel_suite(ops, dev, peak, steps=args.steps, warmup=args.warmup)}), flush=True)
+    emit({"kernels": kernel_suite(ops, dev, peak, steps=args.steps, warmup=args.warmup)})
     return 0
 
 
 def main():
+    # stdout carries exactly one JSON line: everything else (NCCL banners, library
+    # messages, Python prints) goes to stderr, the JSON to the saved stdout.
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)

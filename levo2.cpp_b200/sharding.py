@@ -57,6 +57,7 @@ class HostGather:
             barrier()
             if rank != 0:
                 self.shm = shared_memory.SharedMemory(name=self.name)
+                _untrack(self.shm)
             self.array = np.ndarray(self.shape, dtype=np.float32, buffer=self.shm.buf)
         else:
             self.path = os.path.join(tempfile.gettempdir(), self.name + ".f32")
@@ -97,6 +98,17 @@ class HostGather:
                     pass
         elif self.rank == 0 and self.path and os.path.exists(self.path):
             os.unlink(self.path)
+
+
+def _untrack(shm: shared_memory.SharedMemory) -> None:
+    """Rank 0 owns (and unlinks) the segment; an attaching rank must not have
+    Python's resource tracker unlink it again at exit."""
+    try:
+        from multiprocessing import resource_tracker
+
+        resource_tracker.unregister(shm._name, "shared_memory")  # noqa: SLF001
+    except Exception:
+        pass
 
 
 def _free_bytes(path: str) -> int:
