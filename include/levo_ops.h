@@ -401,6 +401,27 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
                                           int32_t *status, levo_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
+/* next (f3)  greedy next-token selection over LeLM logits                    */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces Sampler::sample_streams with use_sampling = false
+ * (src/levo-sampling.cpp:127-154, sample_top_k_counted :74-97): for each row
+ * (stream) of `vocab` logits (row stride ld),
+ *   1. each distinct id of recent[row][0..recent_len) in [0, penalty_limit)
+ *      divides its logit once by `penalty` (:39-48; penalty_limit <= 0 means
+ *      vocab; the reference passes vocab - 1 so the EOS id is exempt; ids < 0
+ *      are skipped, so rows can be padded with -1);
+ *   2. row 0 only: ids in ignore[0..n_ignore) become -inf (:146-148);
+ *   3. tokens_out[row] = index of the first maximum (std::max_element).
+ * Bit-exact with the reference.  recent may be NULL.  status (optional device
+ * int32): bit 1 set when a logit is NaN (the reference throws).  vocab <= 131072.
+ */
+LEVO_OPS_API int levo_greedy_tokens_f32(const float *logits, int64_t rows, int64_t vocab, int64_t ld,
+                                        const int64_t *recent, int64_t recent_len, float penalty,
+                                        int64_t penalty_limit, const int64_t *ignore, int64_t n_ignore,
+                                        int64_t *tokens_out, int32_t *status, levo_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
 /* next (f1)  window assembly: crossfade + crop (+ interleave)                */
 /* ------------------------------------------------------------------------- */
 /*

@@ -142,6 +142,7 @@ SIGNATURES = {
     "levo_cfg_euler_multi_f32": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _F, _F, _P, _P]),
     "levo_gated_layernorm_modulate_f32": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F, _P]),
     "levo_vae_decode_noalloc_f32": (_INT, [ctypes.POINTER(Topology), _P, _P, _I64, _P, CONV_FN, _P, _U32, _P]),
+    "levo_greedy_tokens_f32": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P, _P, _P]),
     "levo_assemble_windows_f32": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P]),
 }
 
@@ -362,6 +363,20 @@ def assemble_windows_t(windows, hop_samples: int, overlap_samples: int, target_s
         out = torch.empty(shape, dtype=torch.float32, device=windows.device)
     check(lib().levo_assemble_windows_f32(_ptr(windows), w, c, s, hop_samples, overlap_samples, target_samples,
                                           _ptr(out), 1 if interleaved else 0, _stream(windows.device)))
+    return out
+
+
+def greedy_tokens_t(logits, recent=None, penalty=1.0, penalty_limit=0, ignore=None, status=None, out=None):
+    """Greedy next token per row of logits [rows, vocab] (reference sample_streams, use_sampling=False)."""
+    import torch
+
+    _require_cuda(logits, recent, ignore, status, out)
+    rows, vocab = logits.shape
+    out = torch.empty(rows, dtype=torch.int64, device=logits.device) if out is None else out
+    recent_len = recent.shape[1] if recent is not None else 0
+    check(lib().levo_greedy_tokens_f32(_ptr(logits), rows, vocab, logits.stride(0), _ptr(recent), recent_len, penalty,
+                                       penalty_limit, _ptr(ignore), ignore.numel() if ignore is not None else 0,
+                                       _ptr(out), _ptr(status), _stream(logits.device)))
     return out
 
 

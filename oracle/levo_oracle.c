@@ -569,3 +569,42 @@ int oracle_assemble_windows_f32(const float *windows, int64_t n, int64_t channel
     free(full);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* greedy token selection                                                    */
+/* ------------------------------------------------------------------------ */
+
+int oracle_greedy_tokens_f32(const float *logits, int64_t rows, int64_t vocab, const int64_t *recent,
+                             int64_t recent_len, float penalty, int64_t penalty_limit,
+                             const int64_t *ignore, int64_t n_ignore, int64_t *out) {
+    if (!logits || !out || rows < 0 || vocab <= 0) return -2;
+    const int64_t limit = penalty_limit <= 0 ? vocab : (penalty_limit < vocab ? penalty_limit : vocab);
+    float *row = (float *)malloc(sizeof(float) * (size_t)vocab);
+    unsigned char *seen = (unsigned char *)malloc((size_t)vocab);
+    if (!row || !seen) return -2;
+    int rc = 0;
+    for (int64_t r = 0; r < rows; ++r) {
+        memcpy(row, logits + r * vocab, sizeof(float) * (size_t)vocab);
+        memset(seen, 0, (size_t)vocab);
+        /* unique recent ids, each divided once (:39-48) */
+        for (int64_t k = 0; recent && k < recent_len; ++k) {
+            const int64_t t = recent[r * recent_len + k];
+            if (t >= 0 && t < limit && !seen[t]) {
+                seen[t] = 1;
+                row[t] /= penalty;
+            }
+        }
+        /* ignore list on the first stream (:146-148) */
+        for (int64_t k = 0; r == 0 && ignore && k < n_ignore; ++k)
+            if (ignore[k] >= 0 && ignore[k] < vocab) row[ignore[k]] = -INFINITY;
+        int64_t best = 0;
+        for (int64_t i = 0; i < vocab; ++i) {
+            if (isnan(row[i])) rc = -1;
+            else if (isnan(row[best]) || row[i] > row[best]) best = i; /* first maximum */
+        }
+        out[r] = best;
+    }
+    free(row);
+    free(seen);
+    return rc;
+}

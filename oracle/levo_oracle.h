@@ -103,6 +103,13 @@ int oracle_assemble_windows_f32(const float *windows, int64_t n, int64_t channel
                                 int64_t window_samples, int64_t hop, int64_t overlap,
                                 int64_t target, float *out);
 
+/* Greedy token per row, restating sample_streams with use_sampling = false
+ * (src/levo-sampling.cpp:39-48,74-97,127-154).  Returns -1 when a logit is NaN
+ * (the reference throws); the indices are still written. */
+int oracle_greedy_tokens_f32(const float *logits, int64_t rows, int64_t vocab, const int64_t *recent,
+                             int64_t recent_len, float penalty, int64_t penalty_limit,
+                             const int64_t *ignore, int64_t n_ignore, int64_t *out);
+
 /* IEEE half <-> float (round to nearest even). */
 float oracle_half_to_float(uint16_t h);
 uint16_t oracle_float_to_half(float f);

@@ -38,11 +38,14 @@ _SIGS = {
     "oracle_cfg_combine_f32": [_P, _P, _P, _I64, _F],
     "oracle_gated_layernorm_modulate_f32": [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F],
     "oracle_assemble_windows_f32": [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P],
+    "oracle_greedy_tokens_f32": [_P, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P],
     "oracle_cfg_euler_f32": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _F, _F],
 }
 
 _REF_SIGS = {
     "ref_last_error": (ctypes.c_char_p, []),
+    "ref_sample_streams_greedy": (_INT, [_P, _I64, _I64, _P, _I64, _F, _P, _I64, _P]),
+    "ref_apply_cfg": (_INT, [_P, _P, _I64, _F, _P]),
     "ref_combine_renderer_cfg": (_INT, [_P, _P, _I64, _F, _P]),
     "ref_solve_flow_euler": (_INT, [_P, _P, _I64, _I64, _I64, _F, _I64, _P, _P, _INT, _F, _I64, _P, _I64, _P, _P,
                                     ctypes.POINTER(_I64)]),
@@ -241,6 +244,19 @@ def assemble_windows(windows, hop, overlap, target) -> np.ndarray:
     return out
 
 
+def greedy_tokens(logits, recent=None, penalty=1.0, penalty_limit=0, ignore=None):
+    """Returns (tokens, ok); ok is False when a logit is NaN."""
+    x = _f32(logits)
+    rows, vocab = x.shape
+    rec = None if recent is None else np.ascontiguousarray(recent, dtype=np.int64)
+    ign = None if ignore is None else np.ascontiguousarray(ignore, dtype=np.int64)
+    out = np.empty(rows, np.int64)
+    rc = lib().oracle_greedy_tokens_f32(_p(x), rows, vocab, _p(rec), 0 if rec is None else rec.shape[1], penalty,
+                                        penalty_limit, _p(ign), 0 if ign is None else ign.size, _p(out))
+    assert rc in (0, -1)
+    return out, rc == 0
+
+
 # --------------------------------------------------------------------------- reference (compiled sources)
 
 def _ref_err() -> str:
@@ -300,3 +316,25 @@ def ref_make_renderer_euler_schedule(steps: int):
     if ref().ref_make_renderer_euler_schedule(steps, _p(times), ctypes.byref(dt)) != 0:
         raise ValueError(_ref_err())
     return times, dt.value
+
+
+def ref_sample_streams_greedy(logits, recent=None, penalty=1.0, ignore=None):
+    """The reference's Sampler::sample_streams(use_sampling=False): penalty over each full
+    recent row (window = its length), ignore list on stream 0, vocabulary limit = vocab - 1."""
+    x = _f32(logits)
+    rows, vocab = x.shape
+    rec = None if recent is None else np.ascontiguousarray(recent, dtype=np.int64)
+    ign = None if ignore is None else np.ascontiguousarray(ignore, dtype=np.int64)
+    out = np.empty(rows, np.int64)
+    if ref().ref_sample_streams_greedy(_p(x), rows, vocab, _p(rec), 0 if rec is None else rec.shape[1], penalty,
+                                       _p(ign), 0 if ign is None else ign.size, _p(out)) != 0:
+        raise ValueError(_ref_err())
+    return out
+
+
+def ref_apply_cfg(cond, uncond, scale):
+    c, u = _f32(cond), _f32(uncond)
+    out = np.empty_like(c)
+    if ref().ref_apply_cfg(_p(c), _p(u), c.size, scale, _p(out)) != 0:
+        raise ValueError(_ref_err())
+    return out

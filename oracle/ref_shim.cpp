@@ -12,6 +12,7 @@
 
 #include "levo-flow-renderer.h"
 #include "levo-renderer-pattern.h"
+#include "levo-sampling.h"
 
 #define REF_API extern "C" __attribute__((visibility("default")))
 
@@ -151,6 +152,49 @@ REF_API int ref_make_renderer_euler_schedule(int64_t steps, float *times, float 
         const levo::renderer_euler_schedule s = levo::make_renderer_euler_schedule(static_cast<std::size_t>(steps));
         std::memcpy(times, s.times.data(), s.times.size() * sizeof(float));
         *dt = s.dt;
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
+}
+
+// Sampler::sample_streams with use_sampling = false (src/levo-sampling.cpp:127-154).
+// recent: [rows][recent_len] (entries < 0 are dropped, so rows may be padded),
+// the repetition window is recent_len; ignore applies to stream 0.
+REF_API int ref_sample_streams_greedy(const float *logits, int64_t rows, int64_t vocab, const int64_t *recent,
+                                      int64_t recent_len, float penalty, const int64_t *ignore,
+                                      int64_t n_ignore, int64_t *out) {
+    try {
+        std::vector<levo::logits> streams(static_cast<std::size_t>(rows));
+        std::vector<std::vector<int64_t>> rec;
+        for (int64_t r = 0; r < rows; ++r) {
+            streams[r].assign(logits + r * vocab, logits + (r + 1) * vocab);
+            if (recent) {
+                std::vector<int64_t> row;
+                for (int64_t k = 0; k < recent_len; ++k)
+                    if (recent[r * recent_len + k] >= 0) row.push_back(recent[r * recent_len + k]);
+                rec.push_back(row);
+            }
+        }
+        levo::sampling_config config;
+        config.use_sampling = false;
+        config.repetition_penalty = penalty;
+        config.repetition_window = static_cast<std::size_t>(recent_len);
+        if (ignore) config.ignore_tokens.assign(ignore, ignore + n_ignore);
+        levo::Sampler sampler(0);
+        const std::vector<int64_t> tokens = sampler.sample_streams(streams, config, rec);
+        std::memcpy(out, tokens.data(), tokens.size() * sizeof(int64_t));
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
+}
+
+// apply_cfg (src/levo-sampling.cpp:21-27): unconditional + scale * (conditional - unconditional).
+REF_API int ref_apply_cfg(const float *cond, const float *uncond, int64_t n, float scale, float *out) {
+    try {
+        const levo::logits r = levo::apply_cfg(levo::logits(cond, cond + n), levo::logits(uncond, uncond + n), scale);
+        std::memcpy(out, r.data(), r.size() * sizeof(float));
         return 0;
     } catch (const std::exception &e) {
         return fail(e);

@@ -292,3 +292,38 @@ def test_gated_layernorm_modulate_matches_definition(orc):
     want = (n * gamma + beta) * (1 + scale[b]) + shift[b]
     assert_close(h, hh, 1e-6)
     assert_close(y, want, 1e-5)
+
+
+# --------------------------------------------------------------------------- greedy token selection (next item)
+
+def test_greedy_known_answers(orc):
+    # tests/test-sampling.cpp:12-15: token 2 is penalised, the EOS (last) logit is exempt
+    tok, ok = orc.greedy_tokens(np.array([[9, 8, 10, 7]], np.float32), recent=np.array([[2, 3]]), penalty=2.0,
+                                penalty_limit=3)
+    assert ok and tok.tolist() == [0]
+    # tests/test-sampling.cpp:36: greedy streams pick the first maximum per stream
+    tok, ok = orc.greedy_tokens(np.array([[0, 2, 1], [1, 4, 0]], np.float32))
+    assert ok and tok.tolist() == [1, 1]
+    # tests/test-sampling.cpp:8: LM-side CFG uses the same combine as the renderer
+    assert np.array_equal(orc.cfg_combine([1, 1], [2, 4], 1.5), np.array([2.5, 5.5], np.float32))
+
+
+@needs_ref
+def test_greedy_oracle_matches_reference_code():
+    import __graft_entry__ as entry
+
+    orc = entry.load_oracle()
+    rng = np.random.default_rng(11)
+    vocab = 16385
+    for trial in range(6):
+        x = rng.standard_normal((3, vocab)).astype(np.float32)
+        x[:, rng.integers(0, vocab, 40)] = x.max() + 1.0  # ties at the maximum
+        if trial == 3:
+            x[1] = -np.inf
+        recent = rng.integers(-1, vocab, (3, 50))
+        ignore = rng.integers(0, vocab, 8)
+        want = orc.ref_sample_streams_greedy(x, recent, 1.1, ignore)
+        got, ok = orc.greedy_tokens(x, recent, 1.1, vocab - 1, ignore)
+        assert ok and np.array_equal(got, want)
+    u, c = rng.standard_normal((2, 999)).astype(np.float32)
+    assert np.array_equal(orc.ref_apply_cfg(c, u, 1.5), orc.cfg_combine(u, c, 1.5))
