@@ -1,0 +1,170 @@
+// levo_ops.hpp — C++ face of liblevo_b200.so for the reference's C++ callers.
+//
+// Header-only wrappers over the C ABI of levo_ops.h.  They keep the names and
+// the error behaviour of the reference's operators, so a call site in
+// LeVo2.cpp changes its arguments (device pointers instead of ggml_tensor*),
+// not its structure or its exception handling:
+//   invalid arguments  -> std::invalid_argument("LeVo audio graph: ...")   (src/levo-audio-ops.cpp:45-47)
+//   Flow-side checks   -> std::invalid_argument with the reference's wording (src/levo-renderer-pattern.cpp:127-130)
+//   non-finite Euler   -> std::runtime_error("LeVo Flow renderer: ...")    (src/levo-flow-renderer.cpp:13-15,24-28)
+//   cancellation       -> levo::b200::operation_cancelled                 (include/levo.h:21-24)
+//   anything else      -> std::runtime_error with the library's message
+// All tensors are device pointers in the reference's layouts (activations
+// [channels][time], rows [rows][dim], Flow state [frames][latent_dim]).
+#ifndef LEVO_OPS_HPP
+#define LEVO_OPS_HPP
+
+#include <cstdint>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "levo_ops.h"
+
+namespace levo::b200 {
+
+class operation_cancelled : public std::runtime_error {
+   public:
+    operation_cancelled() : std::runtime_error("LeVo operation cancelled") {}
+};
+
+namespace detail {
+inline void check(int rc, const char *domain) {
+    if (rc == LEVO_OPS_OK) return;
+    const std::string msg = std::string(domain) + levo_ops_last_error();
+    if (rc == LEVO_OPS_EINVAL) throw std::invalid_argument(msg);
+    if (rc == LEVO_OPS_ECANCELLED) throw operation_cancelled();
+    throw std::runtime_error(msg);
+}
+constexpr const char *kAudio = "LeVo audio graph: ";
+constexpr const char *kFlow = "LeVo Flow renderer: ";
+constexpr const char *kVae = "LeVo VAE: ";
+}  // namespace detail
+
+// levo::detail::snake_beta (src/levo-audio-ops.cpp:160-187): y = x + sin(x*e^a)^2 / (e^b + 1e-9).
+inline void snake_beta(const float *x, const float *alpha_log, const float *beta_log, float *y,
+                       int64_t channels, int64_t time, levo_stream_t stream = nullptr) {
+    detail::check(levo_snakebeta_f32(x, time, alpha_log, beta_log, LEVO_DTYPE_F32, y, time, channels, time,
+                                     stream),
+                  detail::kAudio);
+}
+
+// One run_residual / stage node run (src/levo-vae.cpp:90-101), fused.
+inline void fused_unit(const levo_fused_unit &unit, levo_stream_t stream = nullptr) {
+    detail::check(levo_vae_fused_unit_f32(&unit, stream), detail::kAudio);
+}
+
+// rms_norm_weighted + residual add (src/levo-lm.cpp:131-138,198-202), F16 activations.
+inline void add_rms_norm_f16(const void *x, const void *residual, const float *gamma, void *h_out, void *y_out,
+                             int64_t rows, int64_t dim, float eps, bool f16_boundary,
+                             levo_stream_t stream = nullptr) {
+    detail::check(levo_add_rmsnorm_f16(x, residual, gamma, h_out, y_out, rows, dim, eps,
+                                       f16_boundary ? LEVO_NORM_F16_BOUNDARY : 0u, stream),
+                  detail::kAudio);
+}
+
+// layer_norm + residual add (src/levo-flow-estimator.cpp:106-109,221-227), F32 activations.
+inline void add_layer_norm_f32(const float *x, const float *residual, const float *gamma, const float *beta,
+                               float *h_out, float *y_out, int64_t rows, int64_t dim, float eps = 1.0e-5f,
+                               levo_stream_t stream = nullptr) {
+    detail::check(levo_add_layernorm_f32(x, residual, gamma, beta, h_out, y_out, rows, dim, eps, 0u, stream),
+                  detail::kAudio);
+}
+
+// combine_renderer_cfg (src/levo-renderer-pattern.cpp:123-135), device vectors.
+inline void combine_renderer_cfg(const float *unconditional, const float *conditional, float *out, int64_t n,
+                                 float guidance_scale, levo_stream_t stream = nullptr) {
+    const int rc = levo_cfg_combine_f32(unconditional, conditional, out, n, guidance_scale, stream);
+    if (rc == LEVO_OPS_EINVAL) {
+        // the reference's own messages, without a domain prefix
+        if (n <= 0) throw std::invalid_argument("CFG vectors must have equal non-empty lengths");
+        throw std::invalid_argument("CFG guidance scale must be finite");
+    }
+    detail::check(rc, detail::kFlow);
+}
+
+// One step of solve_flow_euler (src/levo-flow-renderer.cpp:93-106) on device
+// state [frames][latent_dim]: in-context interpolation, then the caller's
+// velocity callback (the estimator), then the fused CFG + Euler update.  The
+// velocity callback returns a device pointer to [2][frames*latent_dim]
+// (row 0 unconditional, row 1 conditional) when cfg, else [frames*latent_dim].
+struct euler_device_input {
+    float *state;              // in/out
+    const float *noise;        // [frames*latent_dim]
+    const float *context;      // [frames*latent_dim]
+    int64_t frames = 0;
+    int64_t latent_dim = 0;
+    int64_t incontext_frames = 0;
+    float sigma_min = 1.0e-4f;
+};
+
+template <class Velocity, class Cancelled>
+void solve_flow_euler(const euler_device_input &in, int64_t steps, bool cfg, float guidance,
+                      Velocity &&velocity, Cancelled &&cancelled, int32_t *status_dev,
+                      int64_t completed_steps = 0, levo_stream_t stream = nullptr) {
+    if (steps <= 0) throw std::runtime_error("LeVo Flow renderer: Euler step count must be positive");
+    if (in.incontext_frames > in.frames)
+        throw std::runtime_error("LeVo Flow renderer: Euler in-context length exceeds frame count");
+    const int64_t n = in.frames * in.latent_dim;
+    for (int64_t step = completed_steps; step < steps; ++step) {
+        if (cancelled()) throw operation_cancelled();
+        if (in.incontext_frames > 0)
+            detail::check(levo_flow_incontext_f32(in.state, in.noise, in.context, 1, n,
+                                                  in.incontext_frames * in.latent_dim, step, steps, in.sigma_min,
+                                                  stream),
+                          detail::kFlow);
+        const float *v = velocity(static_cast<const float *>(in.state), step);
+        detail::check(levo_euler_cfg_step_f32(in.state, v, cfg ? v + n : nullptr, n, cfg ? 1 : 0, guidance, steps,
+                                              status_dev, stream),
+                      detail::kFlow);
+    }
+    // Final context restore (src/levo-flow-renderer.cpp:113-114): a zero-step
+    // multi-step call at the end of the solve restores the prefix only.
+    detail::check(levo_cfg_euler_multi_f32(in.state, in.noise, in.context, nullptr, nullptr, 1, n,
+                                           in.incontext_frames * in.latent_dim, steps, 0, steps, 0, 1.0f,
+                                           in.sigma_min, nullptr, stream),
+                  detail::kFlow);
+}
+
+// vae_decoder (src/levo-vae.h:21-43) over the elementwise chain.
+class vae_decoder {
+   public:
+    vae_decoder(const levo_vae_topology &topology, const std::vector<float> &packed_params, int64_t max_frames,
+                int device = 0, levo_conv_fn conv = nullptr, void *conv_user = nullptr) {
+        levo_vae_chain *chain = nullptr;
+        detail::check(levo_vae_chain_create(&chain, &topology, packed_params.data(), max_frames, conv, conv_user,
+                                            device),
+                      detail::kVae);
+        chain_.reset(chain);
+        topology_ = topology;
+    }
+
+    // Host latent [latent_dim][frames] -> host audio [audio_channels][frames * prod(strides)],
+    // like vae_decoder::decode (src/levo-vae.cpp:172-276).
+    std::vector<float> decode(const std::vector<float> &latent, int64_t frames, bool tanh = false,
+                              levo_stream_t stream = nullptr) const {
+        int64_t up = 1;
+        for (int s = 0; s < topology_.n_stages; ++s) up *= topology_.stage_stride[s];
+        if (frames <= 0 || static_cast<int64_t>(latent.size()) != frames * topology_.latent_dim)
+            throw std::runtime_error("LeVo VAE: latent payload does not have shape [64,frames]");
+        std::vector<float> audio(static_cast<size_t>(topology_.audio_channels * frames * up));
+        detail::check(levo_vae_chain_decode_windows(chain_.get(), latent.data(), 1, frames, audio.data(),
+                                                    tanh ? LEVO_CHAIN_TANH : 0u, nullptr, nullptr, stream),
+                      detail::kVae);
+        return audio;
+    }
+
+    levo_vae_chain *handle() const noexcept { return chain_.get(); }
+
+   private:
+    struct deleter {
+        void operator()(levo_vae_chain *c) const noexcept { levo_vae_chain_destroy(c); }
+    };
+    std::unique_ptr<levo_vae_chain, deleter> chain_;
+    levo_vae_topology topology_{};
+};
+
+}  // namespace levo::b200
+
+#endif  // LEVO_OPS_HPP
