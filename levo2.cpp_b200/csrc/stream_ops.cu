@@ -23,6 +23,10 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 2;
+// Rows form: 128-thread CTAs, one vector per thread per chunk for the 2-input
+// residual unit and two for the 1-input units (the fastest shape in a sweep of
+// block size 128-512 and unroll 1-8 on the config-4 chain).
+constexpr int kRowThreads = 128;
 constexpr int64_t kMaxStagedChannels = 4096;
 
 struct StreamArgs {
@@ -107,7 +111,7 @@ __device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelPar
 // Rows form: CTA b owns chunks [b*chunks/G, (b+1)*chunks/G); chunk q covers
 // vectors [k*kThreads*UNROLL, (k+1)*kThreads*UNROLL) of row c, q = c*cpr + k.
 template <bool HAS_RES, bool SNAKE, int UNROLL>
-__global__ void __launch_bounds__(kThreads) stream_rows_kernel(const StreamArgs a) {
+__global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamArgs a) {
     const int64_t q0 = a.chunks * blockIdx.x / gridDim.x;
     const int64_t q1 = a.chunks * (blockIdx.x + 1) / gridDim.x;
     if (q0 >= q1) return;
@@ -116,11 +120,11 @@ __global__ void __launch_bounds__(kThreads) stream_rows_kernel(const StreamArgs 
     ChannelParams p = channel_params<SNAKE>(a, nullptr, c);
     for (int64_t q = q0; q < q1; ++q) {
         const size_t row = static_cast<size_t>(c) * a.len;
-        const int64_t v0 = k * (kThreads * UNROLL) + threadIdx.x;
+        const int64_t v0 = k * (kRowThreads * UNROLL) + threadIdx.x;
         f32x8 uu[UNROLL], rr[UNROLL];
 #pragma unroll
         for (int j = 0; j < UNROLL; ++j) {
-            const int64_t v = v0 + j * kThreads;
+            const int64_t v = v0 + j * kRowThreads;
             if (v < a.vec_per_row) {
                 uu[j] = ld8(a.u + row + v * 8);
                 if (HAS_RES) rr[j] = ld8(a.res + row + v * 8);
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kThreads) stream_rows_kernel(const StreamArgs 
         }
 #pragma unroll
         for (int j = 0; j < UNROLL; ++j) {
-            const int64_t v = v0 + j * kThreads;
+            const int64_t v = v0 + j * kRowThreads;
             if (v >= a.vec_per_row) continue;
             f32x8 xo, yo;
             unit_eval8<HAS_RES, SNAKE>(a, p, uu[j], rr[j], xo, yo);
@@ -244,19 +248,19 @@ __global__ void __launch_bounds__(kThreads) stream_scalar_kernel(const StreamArg
 
 template <bool HAS_RES, bool SNAKE>
 int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
-    constexpr int kRowUnroll = HAS_RES ? 2 : 4;
+    constexpr int kRowUnroll = HAS_RES ? 1 : 2;
     auto kernel = stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll>;
     a.staged = 0;
     a.vec_per_row = a.len / 8;
-    a.chunks_per_row = (a.vec_per_row + kThreads * kRowUnroll - 1) / (kThreads * kRowUnroll);
+    a.chunks_per_row = (a.vec_per_row + kRowThreads * kRowUnroll - 1) / (kRowThreads * kRowUnroll);
     a.chunks = a.rows * a.chunks_per_row;
     a.inv_chunks_per_row = 1.0 / static_cast<double>(a.chunks_per_row);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kRowThreads, 0) != cudaSuccess ||
         per_sm <= 0)
         per_sm = 1;
     const int64_t grid = std::min<int64_t>(a.chunks, static_cast<int64_t>(sm_count()) * per_sm);
-    kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(a);
+    kernel<<<static_cast<unsigned>(grid), kRowThreads, 0, stream>>>(a);
     return check_launch(what);
 }
 
