@@ -199,6 +199,15 @@ typedef struct levo_vae_chain levo_vae_chain;
 LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topology *topology,
                                        const float *params_host, int64_t max_frames,
                                        levo_conv_fn conv, void *conv_user, int device);
+/*
+ * Same, with the packed parameters stored as IEEE F16 (the reference's F16 VAE
+ * artifact, tools/levo-quantize.cpp:286-312): they stay F16 in HBM and every
+ * fused unit promotes them to F32 in-kernel, as the reference's graph casts
+ * each F16 weight to F32 before its node (src/levo-audio-ops.cpp:67-72).
+ */
+LEVO_OPS_API int levo_vae_chain_create_f16(levo_vae_chain **out, const levo_vae_topology *topology,
+                                           const uint16_t *params_host, int64_t max_frames,
+                                           levo_conv_fn conv, void *conv_user, int device);
 LEVO_OPS_API void levo_vae_chain_destroy(levo_vae_chain *chain);
 
 #define LEVO_CHAIN_TANH 1u    /* tanh epilogue on the audio (BASELINE option; the reference has none) */
@@ -399,6 +408,27 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
                                           int64_t first_step, int64_t count, int64_t steps,
                                           int32_t cfg, float guidance, float sigma_min,
                                           int32_t *status, levo_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* next (f2)  latent normalisation and the layout change into the VAE         */
+/* ------------------------------------------------------------------------- */
+/*
+ * channel_major[c][f] = frame_major[f][c] * stddev[c] + mean[c]
+ * Replaces denormalize_latents (src/levo-flow-conditioning.cpp:125-135)
+ * followed by channel_major_latent (src/levo-render.cpp:181-193): the Flow
+ * renderer's frame-major [frames][dim] window becomes the VAE's channel-major
+ * [dim][frames] input in one pass.  mean and stddev both NULL: transpose only.
+ * Not in place.  Bit-identical to the reference (mul then add, no FMA).
+ */
+LEVO_OPS_API int levo_latent_to_vae_f32(const float *frame_major, const float *mean, const float *stddev,
+                                        int64_t frames, int64_t dim, float *channel_major,
+                                        levo_stream_t stream);
+/*
+ * normalized[f][c] = (raw[f][c] - mean[c]) / stddev[c], frame-major
+ * (normalize_latents, src/levo-flow-conditioning.cpp:113-123).  May run in place.
+ */
+LEVO_OPS_API int levo_latent_normalize_f32(const float *raw, const float *mean, const float *stddev,
+                                           int64_t frames, int64_t dim, float *normalized, levo_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* next (f3)  greedy next-token selection over LeLM logits                    */

@@ -85,8 +85,8 @@ __global__ void __launch_bounds__(256) conv_standin_vec8_kernel(const float *in,
 }
 
 struct SnakeRef {
-    const float *alpha;
-    const float *beta;
+    const void *alpha;
+    const void *beta;
 };
 
 struct StageOffsets {
@@ -194,7 +194,8 @@ struct levo_vae_chain {
     levo::Layout layout{};
     int64_t max_frames = 0;
     int64_t max_elems = 0;
-    float *params = nullptr;
+    void *params = nullptr;       // packed parameters, F32 or F16 (pdtype)
+    int pdtype = LEVO_DTYPE_F32;
     float *X = nullptr;
     float *A = nullptr;
     float *B = nullptr;
@@ -316,15 +317,17 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
                uint32_t flags, cudaStream_t s) {
     const levo_vae_topology &t = c->topo;
     const Layout &l = c->layout;
-    const float *P = c->params;
+    const size_t esize = c->pdtype == LEVO_DTYPE_F16 ? 2 : 4;
+    const char *base = static_cast<const char *>(c->params);
+    auto P = [&](int64_t off) -> const void * { return base + off * esize; };
     const bool timing = (flags & LEVO_CHAIN_TIMING) != 0;
     auto snake_of = [&](int stage, int unit) -> SnakeRef {
         // Activation applied before conv `unit` of `stage`; unit == n_residual
         // means the next stage's upsample activation (or the output one).
         if (stage < t.n_stages && unit < t.n_residual)
-            return {P + l.stage[stage].pre_alpha[unit], P + l.stage[stage].pre_beta[unit]};
-        if (stage + 1 < t.n_stages) return {P + l.stage[stage + 1].up_alpha, P + l.stage[stage + 1].up_beta};
-        return {P + l.out_alpha, P + l.out_beta};
+            return {P(l.stage[stage].pre_alpha[unit]), P(l.stage[stage].pre_beta[unit])};
+        if (stage + 1 < t.n_stages) return {P(l.stage[stage + 1].up_alpha), P(l.stage[stage + 1].up_beta)};
+        return {P(l.out_alpha), P(l.out_beta)};
     };
 
     // Input conv + ENTRY unit.
@@ -348,13 +351,13 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
     {
         levo_fused_unit u{};
         u.u = cur;
-        u.bias = P + l.in_bias;
-        u.alpha_log = P + l.stage[0].up_alpha;
-        u.beta_log = P + l.stage[0].up_beta;
+        u.bias = P(l.in_bias);
+        u.alpha_log = P(l.stage[0].up_alpha);
+        u.beta_log = P(l.stage[0].up_beta);
         u.y_out = cur;
         u.channels = t.entry_width;
         u.time = frames;
-        u.param_dtype = LEVO_DTYPE_F32;
+        u.param_dtype = c->pdtype;
         rc = run_unit(c, timing, LEVO_KCLASS_ENTRY, u, s);
         if (rc != LEVO_OPS_OK) return rc;
     }
@@ -386,14 +389,14 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
             const SnakeRef sn = snake_of(st, 0);
             levo_fused_unit u{};
             u.u = cur;
-            u.bias = P + so.up_bias;
+            u.bias = P(so.up_bias);
             u.alpha_log = sn.alpha;
             u.beta_log = sn.beta;
             u.x_out = t.n_residual > 0 ? c->X : nullptr;
             u.y_out = cur;
             u.channels = cout;
             u.time = lout;
-            u.param_dtype = LEVO_DTYPE_F32;
+            u.param_dtype = c->pdtype;
             rc = run_unit(c, timing, LEVO_KCLASS_UPSAMPLE, u, s);
             if (rc != LEVO_OPS_OK) return rc;
         }
@@ -418,13 +421,13 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
             {
                 levo_fused_unit u{};
                 u.u = cur;
-                u.bias = P + so.bias0[r];
-                u.alpha_log = P + so.post_alpha[r];
-                u.beta_log = P + so.post_beta[r];
+                u.bias = P(so.bias0[r]);
+                u.alpha_log = P(so.post_alpha[r]);
+                u.beta_log = P(so.post_beta[r]);
                 u.y_out = cur;
                 u.channels = cout;
                 u.time = lout;
-                u.param_dtype = LEVO_DTYPE_F32;
+                u.param_dtype = c->pdtype;
                 rc = run_unit(c, timing, LEVO_KCLASS_POST, u, s);
                 if (rc != LEVO_OPS_OK) return rc;
             }
@@ -449,7 +452,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
                 const SnakeRef sn = snake_of(st, r + 1);
                 levo_fused_unit u{};
                 u.u = cur;
-                u.bias = P + so.bias1[r];
+                u.bias = P(so.bias1[r]);
                 u.residual = c->X;
                 u.alpha_log = sn.alpha;
                 u.beta_log = sn.beta;
@@ -457,7 +460,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
                 u.y_out = cur;
                 u.channels = cout;
                 u.time = lout;
-                u.param_dtype = LEVO_DTYPE_F32;
+                u.param_dtype = c->pdtype;
                 rc = run_unit(c, timing, LEVO_KCLASS_RESIDUAL, u, s);
                 if (rc != LEVO_OPS_OK) return rc;
             }
@@ -491,7 +494,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
         u.y_out = audio_out;
         u.channels = t.audio_channels;
         u.time = len;
-        u.param_dtype = LEVO_DTYPE_F32;
+        u.param_dtype = c->pdtype;
         u.flags = LEVO_FUSED_TANH;
         rc = run_unit(c, timing, LEVO_KCLASS_EPILOGUE, u, s);
         if (rc != LEVO_OPS_OK) return rc;
@@ -569,9 +572,8 @@ LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int
     return check_launch("levo_conv_standin_f32");
 }
 
-LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topology *topology,
-                                       const float *params_host, int64_t max_frames,
-                                       levo_conv_fn conv, void *conv_user, int device) {
+static int create_chain(levo_vae_chain **out, const levo_vae_topology *topology, const void *params_host,
+                        int pdtype, int64_t max_frames, levo_conv_fn conv, void *conv_user, int device) {
     using namespace levo;
     clear_error();
     if (out == nullptr || topology == nullptr || params_host == nullptr)
@@ -588,6 +590,7 @@ LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topo
     levo_vae_chain *c = new (std::nothrow) levo_vae_chain();
     if (c == nullptr) return set_error(LEVO_OPS_ENOMEM, "levo_vae_chain_create: out of host memory");
     c->device = device;
+    c->pdtype = pdtype;
     c->topo = *topology;
     c->layout = make_layout(*topology);
     c->max_frames = max_frames;
@@ -614,7 +617,7 @@ LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topo
 
     DeviceGuard guard(device);
     cudaError_t err = cudaSuccess;
-    const size_t param_bytes = static_cast<size_t>(c->layout.total) * sizeof(float);
+    const size_t param_bytes = static_cast<size_t>(c->layout.total) * (pdtype == LEVO_DTYPE_F16 ? 2 : 4);
     if (err == cudaSuccess) err = cudaMalloc(&c->params, param_bytes);
     if (err == cudaSuccess) err = cudaMalloc(&c->X, act_bytes);
     if (err == cudaSuccess) err = cudaMalloc(&c->A, act_bytes);
@@ -634,6 +637,18 @@ LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topo
     }
     *out = c;
     return LEVO_OPS_OK;
+}
+
+LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topology *topology,
+                                       const float *params_host, int64_t max_frames,
+                                       levo_conv_fn conv, void *conv_user, int device) {
+    return create_chain(out, topology, params_host, LEVO_DTYPE_F32, max_frames, conv, conv_user, device);
+}
+
+LEVO_OPS_API int levo_vae_chain_create_f16(levo_vae_chain **out, const levo_vae_topology *topology,
+                                           const uint16_t *params_host, int64_t max_frames,
+                                           levo_conv_fn conv, void *conv_user, int device) {
+    return create_chain(out, topology, params_host, LEVO_DTYPE_F16, max_frames, conv, conv_user, device);
 }
 
 LEVO_OPS_API void levo_vae_chain_destroy(levo_vae_chain *chain) {

@@ -126,6 +126,7 @@ SIGNATURES = {
     "levo_vae_topology_reference": (_INT, [ctypes.POINTER(Topology)]),
     "levo_vae_param_count": (_I64, [ctypes.POINTER(Topology)]),
     "levo_vae_chain_create": (_INT, [ctypes.POINTER(_P), ctypes.POINTER(Topology), _P, _I64, CONV_FN, _P, _INT]),
+    "levo_vae_chain_create_f16": (_INT, [ctypes.POINTER(_P), ctypes.POINTER(Topology), _P, _I64, CONV_FN, _P, _INT]),
     "levo_vae_chain_destroy": (None, [_P]),
     "levo_vae_chain_decode": (_INT, [_P, _P, _I64, _P, _U32, _P]),
     "levo_vae_chain_decode_windows": (_INT, [_P, _P, _I64, _I64, _P, _U32, CANCEL_FN, _P, _P]),
@@ -143,6 +144,8 @@ SIGNATURES = {
     "levo_gated_layernorm_modulate_f32": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F, _P]),
     "levo_vae_decode_noalloc_f32": (_INT, [ctypes.POINTER(Topology), _P, _P, _I64, _P, CONV_FN, _P, _U32, _P]),
     "levo_greedy_tokens_f32": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P, _P, _P]),
+    "levo_latent_to_vae_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
+    "levo_latent_normalize_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
     "levo_assemble_windows_f32": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P]),
 }
 
@@ -380,6 +383,29 @@ def greedy_tokens_t(logits, recent=None, penalty=1.0, penalty_limit=0, ignore=No
     return out
 
 
+def latent_to_vae_t(frame_major, mean=None, stddev=None, out=None):
+    """[frames, dim] frame-major (normalised) latent -> [dim, frames] de-normalised VAE input."""
+    import torch
+
+    _require_cuda(frame_major, mean, stddev, out)
+    frames, dim = frame_major.shape
+    out = torch.empty((dim, frames), dtype=torch.float32, device=frame_major.device) if out is None else out
+    check(lib().levo_latent_to_vae_f32(_ptr(frame_major), _ptr(mean), _ptr(stddev), frames, dim, _ptr(out),
+                                       _stream(frame_major.device)))
+    return out
+
+
+def latent_normalize_t(raw, mean, stddev, out=None):
+    import torch
+
+    _require_cuda(raw, mean, stddev, out)
+    frames, dim = raw.shape
+    out = torch.empty_like(raw) if out is None else out
+    check(lib().levo_latent_normalize_f32(_ptr(raw), _ptr(mean), _ptr(stddev), frames, dim, _ptr(out),
+                                          _stream(raw.device)))
+    return out
+
+
 def reference_topology() -> Topology:
     t = Topology()
     check(lib().levo_vae_topology_reference(ctypes.byref(t)))
@@ -397,16 +423,19 @@ class VaeChain:
     """Owner of a levo_vae_chain (workspace + parameters on one device)."""
 
     def __init__(self, topology: Topology, params_host, max_frames: int, device: int = 0, conv=None):
+        """params_host: packed parameters as float32, or float16 (kept F16 on the device)."""
         import numpy as np
 
         self.topology = topology
-        self.params = np.ascontiguousarray(params_host, dtype=np.float32)
+        half = getattr(params_host, "dtype", None) == np.float16
+        self.params = np.ascontiguousarray(params_host, dtype=np.float16 if half else np.float32)
         if self.params.size != param_count(topology):
             raise ValueError("parameter array does not match the topology")
         self._conv = CONV_FN(conv) if conv is not None else CONV_FN()
         handle = ctypes.c_void_p()
-        check(lib().levo_vae_chain_create(ctypes.byref(handle), ctypes.byref(topology),
-                                          self.params.ctypes.data, max_frames, self._conv, None, device))
+        create = lib().levo_vae_chain_create_f16 if half else lib().levo_vae_chain_create
+        check(create(ctypes.byref(handle), ctypes.byref(topology), self.params.ctypes.data, max_frames, self._conv,
+                     None, device))
         self.handle = handle
         self.device = device
         self.max_frames = max_frames

@@ -608,3 +608,24 @@ int oracle_greedy_tokens_f32(const float *logits, int64_t rows, int64_t vocab, c
     free(seen);
     return rc;
 }
+
+/* ------------------------------------------------------------------------ */
+/* latent normalisation / layout                                             */
+/* ------------------------------------------------------------------------ */
+
+void oracle_latent_to_vae_f32(const float *frame_major, const float *mean, const float *stddev,
+                              int64_t frames, int64_t dim, float *channel_major) {
+    for (int64_t f = 0; f < frames; ++f)
+        for (int64_t c = 0; c < dim; ++c) {
+            float v = frame_major[f * dim + c];
+            if (mean && stddev) v = v * stddev[c] + mean[c];
+            channel_major[c * frames + f] = v;
+        }
+}
+
+void oracle_latent_normalize_f32(const float *raw, const float *mean, const float *stddev, int64_t frames,
+                                 int64_t dim, float *normalized) {
+    for (int64_t f = 0; f < frames; ++f)
+        for (int64_t c = 0; c < dim; ++c)
+            normalized[f * dim + c] = (raw[f * dim + c] - mean[c]) / stddev[c];
+}

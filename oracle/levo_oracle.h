@@ -110,6 +110,14 @@ int oracle_greedy_tokens_f32(const float *logits, int64_t rows, int64_t vocab, c
                              int64_t recent_len, float penalty, int64_t penalty_limit,
                              const int64_t *ignore, int64_t n_ignore, int64_t *out);
 
+/* denormalize_latents + channel_major_latent (src/levo-flow-conditioning.cpp:125-135,
+ * src/levo-render.cpp:181-193); mean/stddev NULL: transpose only.  And
+ * normalize_latents (src/levo-flow-conditioning.cpp:113-123), frame-major. */
+void oracle_latent_to_vae_f32(const float *frame_major, const float *mean, const float *stddev,
+                              int64_t frames, int64_t dim, float *channel_major);
+void oracle_latent_normalize_f32(const float *raw, const float *mean, const float *stddev, int64_t frames,
+                                 int64_t dim, float *normalized);
+
 /* IEEE half <-> float (round to nearest even). */
 float oracle_half_to_float(uint16_t h);
 uint16_t oracle_float_to_half(float f);

@@ -39,6 +39,8 @@ _SIGS = {
     "oracle_gated_layernorm_modulate_f32": [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F],
     "oracle_assemble_windows_f32": [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P],
     "oracle_greedy_tokens_f32": [_P, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P],
+    "oracle_latent_to_vae_f32": [_P, _P, _P, _I64, _I64, _P],
+    "oracle_latent_normalize_f32": [_P, _P, _P, _I64, _I64, _P],
     "oracle_cfg_euler_f32": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _F, _F],
 }
 
@@ -68,7 +70,8 @@ def lib() -> ctypes.CDLL:
         for name, args in _SIGS.items():
             fn = getattr(h, name)
             fn.argtypes = args
-            fn.restype = None if name == "oracle_conv_standin_f32" else _INT
+            fn.restype = None if name in ("oracle_conv_standin_f32", "oracle_latent_to_vae_f32",
+                                          "oracle_latent_normalize_f32") else _INT
         _lib = h
     return _lib
 
@@ -255,6 +258,23 @@ def greedy_tokens(logits, recent=None, penalty=1.0, penalty_limit=0, ignore=None
                                         penalty_limit, _p(ign), 0 if ign is None else ign.size, _p(out))
     assert rc in (0, -1)
     return out, rc == 0
+
+
+def latent_to_vae(frame_major, mean=None, stddev=None) -> np.ndarray:
+    x = _f32(frame_major)
+    frames, dim = x.shape
+    out = np.empty((dim, frames), np.float32)
+    m = None if mean is None else _f32(mean)
+    s = None if stddev is None else _f32(stddev)
+    lib().oracle_latent_to_vae_f32(_p(x), _p(m), _p(s), frames, dim, _p(out))
+    return out
+
+
+def latent_normalize(raw, mean, stddev) -> np.ndarray:
+    x = _f32(raw)
+    out = np.empty_like(x)
+    lib().oracle_latent_normalize_f32(_p(x), _p(_f32(mean)), _p(_f32(stddev)), x.shape[0], x.shape[1], _p(out))
+    return out
 
 
 # --------------------------------------------------------------------------- reference (compiled sources)

@@ -207,3 +207,20 @@ def test_conv_standin(ops, orc, dev):
     ops.check(ops.lib().levo_conv_standin_f32(torch.from_numpy(x).to(dev).data_ptr(), 6, 11, out.data_ptr(), 4, 33,
                                               3, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     assert np.array_equal(out.cpu().numpy(), orc.conv_standin(x, 4, 33, 3))
+
+
+def test_f16_stored_parameters(ops, orc, dev):
+    # The F16 VAE artifact keeps parameters in F16; each unit promotes them to F32
+    # (src/levo-audio-ops.cpp:67-72): same result as F32 parameters holding the promoted values.
+    topo = small_topology(ops)
+    params16 = params_for(ops, topo, 21).astype(np.float16)
+    frames = 12
+    latent = np.random.default_rng(21).standard_normal((topo.latent_dim, frames)).astype(np.float32)
+    chain16 = ops.VaeChain(topo, params16, max_frames=frames, device=0)
+    chain32 = ops.VaeChain(topo, params16.astype(np.float32), max_frames=frames, device=0)
+    a16 = torch.empty((2, chain16.samples(frames)), device=dev)
+    a32 = torch.empty_like(a16)
+    chain16.decode(torch.from_numpy(latent).to(dev), a16, frames, flags=ops.CHAIN_TANH)
+    chain32.decode(torch.from_numpy(latent).to(dev), a32, frames, flags=ops.CHAIN_TANH)
+    assert torch.equal(a16, a32)
+    assert_close(a16.cpu().numpy(), oracle_audio(orc, topo, params16.astype(np.float32), latent, frames, True), TOL)

@@ -327,3 +327,14 @@ def test_greedy_oracle_matches_reference_code():
         assert ok and np.array_equal(got, want)
     u, c = rng.standard_normal((2, 999)).astype(np.float32)
     assert np.array_equal(orc.ref_apply_cfg(c, u, 1.5), orc.cfg_combine(u, c, 1.5))
+
+
+def test_latent_layout_and_normalisation_definitions(orc):
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((25, 64)).astype(np.float32)
+    mean = rng.standard_normal(64).astype(np.float32)
+    std = rng.uniform(0.5, 2.0, 64).astype(np.float32)
+    assert np.array_equal(orc.latent_to_vae(x), x.T)
+    den = orc.latent_to_vae(x, mean, std)
+    assert np.array_equal(den, ((x * std).astype(np.float32) + mean).astype(np.float32).T)
+    assert np.array_equal(orc.latent_normalize(x, mean, std), ((x - mean).astype(np.float32) / std).astype(np.float32))
