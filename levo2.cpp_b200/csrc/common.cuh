@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "levo_ops.h"
 
@@ -27,6 +28,30 @@ int sm_count();
 
 inline bool aligned_to(const void *p, uintptr_t bytes) {
     return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
+}
+
+// Programmatic dependent launch (sm_90+): the next kernel in the stream may be
+// scheduled while this one drains.  Every kernel launched this way calls
+// pdl_wait() before it reads anything an earlier kernel wrote (a hardware
+// wait for the preceding grid's completion and memory flush; a no-op for a
+// normal launch), then pdl_trigger() to let its own successor be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

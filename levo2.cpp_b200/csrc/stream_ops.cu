@@ -112,6 +112,8 @@ __device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelPar
 // vectors [k*kThreads*UNROLL, (k+1)*kThreads*UNROLL) of row c, q = c*cpr + k.
 template <bool HAS_RES, bool SNAKE, int UNROLL>
 __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t q0 = a.chunks * blockIdx.x / gridDim.x;
     const int64_t q1 = a.chunks * (blockIdx.x + 1) / gridDim.x;
     if (q0 >= q1) return;
@@ -178,6 +180,8 @@ __device__ __forceinline__ void stage_params(const StreamArgs &a, float *smem) {
 template <bool HAS_RES, bool SNAKE>
 __global__ void __launch_bounds__(kThreads) stream_vec8_kernel(const StreamArgs a) {
     extern __shared__ float smem[];
+    pdl_wait();
+    pdl_trigger();
     stage_params<HAS_RES, SNAKE>(a, smem);
 
     // Ragged head and tail (< 8 elements each) go to block 0.
@@ -240,6 +244,8 @@ __global__ void __launch_bounds__(kThreads) stream_vec8_kernel(const StreamArgs 
 template <bool HAS_RES, bool SNAKE>
 __global__ void __launch_bounds__(kThreads) stream_scalar_kernel(const StreamArgs a) {
     extern __shared__ float smem[];
+    pdl_wait();
+    pdl_trigger();
     stage_params<HAS_RES, SNAKE>(a, smem);
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < a.n;
          e += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -260,7 +266,9 @@ int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
         per_sm <= 0)
         per_sm = 1;
     const int64_t grid = std::min<int64_t>(a.chunks, static_cast<int64_t>(sm_count()) * per_sm);
-    kernel<<<static_cast<unsigned>(grid), kRowThreads, 0, stream>>>(a);
+    const cudaError_t err = launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kRowThreads), 0, stream, a);
+    if (err != cudaSuccess)
+        return set_error(LEVO_OPS_ELAUNCH, std::string(what) + ": kernel launch failed: " + cudaGetErrorString(err));
     return check_launch(what);
 }
 
@@ -276,7 +284,10 @@ int launch_variant(const StreamArgs &a, bool vec, size_t smem_bytes, cudaStream_
     const int64_t work_items = vec ? (a.nvec + kUnroll - 1) / kUnroll : a.n;
     const int64_t needed = std::max<int64_t>(1, (work_items + kThreads - 1) / kThreads);
     const int64_t grid = std::min<int64_t>(needed, static_cast<int64_t>(sm_count()) * per_sm);
-    kernel<<<static_cast<unsigned>(grid), kThreads, smem_bytes, stream>>>(a);
+    const cudaError_t err =
+        launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem_bytes, stream, a);
+    if (err != cudaSuccess)
+        return set_error(LEVO_OPS_ELAUNCH, std::string(what) + ": kernel launch failed: " + cudaGetErrorString(err));
     return check_launch(what);
 }
 

@@ -36,6 +36,8 @@ namespace {
 __global__ void __launch_bounds__(256) conv_standin_kernel(const float *in, int64_t cin, int64_t lin,
                                                           float *out, int64_t cout, int64_t lout,
                                                           int32_t stride) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t c = blockIdx.y; c < cout; c += gridDim.y) {
         const float *src = in + (c % cin) * lin;
         float *dst = out + c * lout;
@@ -62,6 +64,8 @@ __global__ void __launch_bounds__(256) conv_standin_vec8_kernel(const float *in,
                                                                int64_t lin, float *out,
                                                                int64_t cout, int64_t lout,
                                                                int32_t stride, double inv_lout) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t nvec = cout * lout / 8;
     for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
          v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -560,14 +564,22 @@ LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (out_length % 8 == 0 && aligned_to(out, 32)) {
         const int64_t grid = std::min<int64_t>((n / 8 + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
-        conv_standin_vec8_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(
-            in, in_channels, in_length, out, out_channels, out_length, stride,
-            1.0 / static_cast<double>(out_length));
+        const cudaError_t err =
+            launch_pdl(conv_standin_vec8_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, s, in,
+                       in_channels, in_length, out, out_channels, out_length, stride,
+                       1.0 / static_cast<double>(out_length));
+        if (err != cudaSuccess)
+            return set_error(LEVO_OPS_ELAUNCH, std::string("levo_conv_standin_f32: kernel launch failed: ") +
+                                                   cudaGetErrorString(err));
     } else {
         const int64_t gx = std::min<int64_t>((out_length + 1023) / 1024, 64);
         const int64_t gy = std::min<int64_t>(out_channels, 65535);
-        conv_standin_kernel<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), 256, 0, s>>>(
-            in, in_channels, in_length, out, out_channels, out_length, stride);
+        const cudaError_t err =
+            launch_pdl(conv_standin_kernel, dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), dim3(256), 0,
+                       s, in, in_channels, in_length, out, out_channels, out_length, stride);
+        if (err != cudaSuccess)
+            return set_error(LEVO_OPS_ELAUNCH, std::string("levo_conv_standin_f32: kernel launch failed: ") +
+                                                   cudaGetErrorString(err));
     }
     return check_launch("levo_conv_standin_f32");
 }
