@@ -191,9 +191,22 @@ __global__ void __launch_bounds__(kThreads) stream_vec8_kernel(const StreamArgs 
         if (threadIdx.x < a.n - tail0) scalar_element<HAS_RES, SNAKE>(a, smem, tail0 + threadIdx.x);
     }
 
+    // Each CTA walks one contiguous range of tiles, so a thread's channel
+    // changes rarely; its parameters are cached in registers by channel.
     const int64_t tile_vecs = static_cast<int64_t>(kThreads) * kUnroll;
-    for (int64_t tile = static_cast<int64_t>(blockIdx.x) * tile_vecs; tile < a.nvec;
-         tile += static_cast<int64_t>(gridDim.x) * tile_vecs) {
+    const int64_t tiles = (a.nvec + tile_vecs - 1) / tile_vecs;
+    const int64_t t0 = tiles * blockIdx.x / gridDim.x;
+    const int64_t t1 = tiles * (blockIdx.x + 1) / gridDim.x;
+    int64_t cached_c = -1;
+    ChannelParams cached{};
+    auto params_for = [&](int64_t c) -> ChannelParams {
+        if (c != cached_c) {
+            cached = channel_params<SNAKE>(a, smem, c);
+            cached_c = c;
+        }
+        return cached;
+    };
+    for (int64_t tile = t0 * tile_vecs; tile < t1 * tile_vecs; tile += tile_vecs) {
         f32x8 uu[kUnroll];
         f32x8 rr[kUnroll];
 #pragma unroll
@@ -215,7 +228,7 @@ __global__ void __launch_bounds__(kThreads) stream_vec8_kernel(const StreamArgs 
                 // At most one row boundary inside the vector.
                 const int64_t c0 = row_of(e, a.len, a.inv_len);
                 const int64_t boundary = (c0 + 1) * a.len;
-                const ChannelParams p0 = channel_params<SNAKE>(a, smem, c0);
+                const ChannelParams p0 = params_for(c0);
                 if (e + 8 <= boundary) {
                     unit_eval8<HAS_RES, SNAKE>(a, p0, uu[j], rr[j], xo, yo);
                 } else {
