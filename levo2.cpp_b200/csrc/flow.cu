@@ -210,14 +210,21 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
     for (int64_t k0 = 0; k0 < a.count; k0 += kStagedSteps) {
         const int cnt = static_cast<int>(a.count - k0 < kStagedSteps ? a.count - k0 : kStagedSteps);
         __syncthreads();  // the previous chunk has been consumed
-        for (int idx = threadIdx.x; idx < 2 * cnt * per_step; idx += kStagedThreads) {
-            const int arr = idx / (cnt * per_step);
-            const int rem = idx - arr * cnt * per_step;
-            const int st = rem / per_step;
-            const int ch = rem - st * per_step;
-            if (ch < full && (arr == 0 || a.cfg)) {
-                const float *src = (arr == 0 ? a.u : a.c) + (k0 + st) * n + i0 + ch * 4;
-                cp_async16(stage + (arr * kStagedSteps + st) * per_step + ch, src);
+        // Thread t copies chunk (t % per_step) of steps t / per_step, + kGroups, ...
+        // for both arrays: no division inside the loop.
+        {
+            constexpr int kGroups = kStagedThreads / (kStagedThreads / 4);  // step rows copied per pass
+            const int ch = threadIdx.x % per_step;
+            const int st0 = threadIdx.x / per_step;
+            if (ch < full) {
+                const float *ub = a.u + (k0 + st0) * n + i0 + ch * 4;
+                const float *cb = a.cfg ? a.c + (k0 + st0) * n + i0 + ch * 4 : nullptr;
+                for (int st = st0; st < cnt; st += kGroups) {
+                    cp_async16(stage + st * per_step + ch, ub);
+                    if (a.cfg) cp_async16(stage + (kStagedSteps + st) * per_step + ch, cb);
+                    ub += kGroups * n;
+                    if (a.cfg) cb += kGroups * n;
+                }
             }
         }
         cp_async_wait_all();
@@ -225,6 +232,7 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
         if (active) {
             const float *su = reinterpret_cast<const float *>(stage);
             const float *sc = su + kStagedSteps * kStagedThreads;
+#pragma unroll 10
             for (int j = 0; j < cnt; ++j) {
                 if (in_prefix) {
                     float t, ns;
