@@ -115,3 +115,18 @@ def test_product_package_does_not_reference_the_oracle():
         text = path.read_text()
         assert "oracle" not in text.lower(), f"{path} mentions the oracle"
         assert "_work/" not in text, path
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """The product path has no fallback: without liblevo_b200.so every call raises."""
+    import subprocess
+    import sys
+
+    code = (
+        "import pathlib, sys; sys.path.insert(0, %r); import __graft_entry__ as e; ops = e.load_package().ops; "
+        "ops.LIB_PATH = pathlib.Path(%r); "
+        "import numpy as np\n"
+        "try:\n    ops.lib()\nexcept ops.LevoOpsError as err:\n    print('raised', err)\n" % (str(ROOT), str(tmp_path / "missing.so"))
+    )
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
+    assert "raised" in out.stdout and "missing" in out.stdout, out.stdout + out.stderr
