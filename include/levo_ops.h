@@ -52,7 +52,11 @@ typedef enum {
 
 typedef enum {
     LEVO_DTYPE_F32 = 0,
-    LEVO_DTYPE_F16 = 1
+    LEVO_DTYPE_F16 = 1,
+    /* SnakeBeta parameters already prepared by levo_snake_params_prepare():
+     * the alpha pointer holds alpha = exp(alpha_log) and the beta pointer holds
+     * 1/beta = 1/(exp(beta_log) + 1e-9), both F32; a bias given with it is F32. */
+    LEVO_DTYPE_SNAKE_PREPARED = 2
 } levo_dtype;
 
 LEVO_OPS_API uint32_t levo_ops_abi_version(void);
@@ -63,12 +67,28 @@ LEVO_OPS_API const char *levo_ops_last_error(void);
 /* a1  SnakeBeta                                                              */
 /* ------------------------------------------------------------------------- */
 /*
+ * Per-channel SnakeBeta parameter precompute, done once per weight load instead
+ * of once per launch: alpha_out[c] = exp(alpha_log[c]) and
+ * inv_beta_out[c] = 1 / (exp(beta_log[c]) + 1e-9), F32, with the same device
+ * arithmetic the kernels apply to log parameters, so a SnakeBeta launch given
+ * the outputs with LEVO_DTYPE_SNAKE_PREPARED is bit-identical to one given the
+ * logs.  The reference recomputes exp(alpha_log) and exp(beta_log) + 1e-9 as
+ * graph nodes on every call (src/levo-audio-ops.cpp:181-185); it has no
+ * separate entry point.  alpha_log / beta_log are F32 or F16 (`param_dtype`).
+ * Zero channels is a no-op.
+ */
+LEVO_OPS_API int levo_snake_params_prepare(const void *alpha_log, const void *beta_log, int param_dtype,
+                                           int64_t channels, float *alpha_out, float *inv_beta_out,
+                                           levo_stream_t stream);
+
+/*
  * y[c][t] = x[c][t] + sin(x[c][t]*alpha_c)^2 / beta_c
  *   alpha_c = exp(alpha_log[c]),  beta_c = exp(beta_log[c]) + 1e-9
  * Replaces levo::detail::snake_beta (src/levo-audio-ops.h:30-33,
  * src/levo-audio-ops.cpp:160-187) as used by run_snake (src/levo-vae.cpp:80-88).
  * alpha_log / beta_log are [channels] in F32 or F16 (`param_dtype`), promoted to
- * F32 in-kernel as the reference's ggml_cast does (src/levo-audio-ops.cpp:67-72).
+ * F32 in-kernel as the reference's ggml_cast does (src/levo-audio-ops.cpp:67-72),
+ * or LEVO_DTYPE_SNAKE_PREPARED outputs of levo_snake_params_prepare().
  * ldx / ldy are row strides in elements (>= time).  Dense rows use the 256-bit
  * vector path; strided rows use the scalar path.
  */
@@ -114,7 +134,7 @@ typedef struct {
     float *y_out;            /* NULL: y is not stored */
     int64_t channels;
     int64_t time;
-    int32_t param_dtype;     /* dtype of bias / alpha_log / beta_log */
+    int32_t param_dtype;     /* dtype of bias / alpha_log / beta_log (SNAKE_PREPARED: F32 bias) */
     uint32_t flags;
 } levo_fused_unit;
 

@@ -50,6 +50,21 @@ inline void snake_beta(const float *x, const float *alpha_log, const float *beta
                   detail::kAudio);
 }
 
+// Per-channel alpha = exp(alpha_log) and 1/beta, computed once per weight load
+// (levo_snake_params_prepare); snake_beta_prepared then gives snake_beta's exact bits.
+inline void snake_params_prepare(const float *alpha_log, const float *beta_log, float *alpha, float *inv_beta,
+                                 int64_t channels, levo_stream_t stream = nullptr) {
+    detail::check(levo_snake_params_prepare(alpha_log, beta_log, LEVO_DTYPE_F32, channels, alpha, inv_beta, stream),
+                  detail::kAudio);
+}
+
+inline void snake_beta_prepared(const float *x, const float *alpha, const float *inv_beta, float *y,
+                                int64_t channels, int64_t time, levo_stream_t stream = nullptr) {
+    detail::check(levo_snakebeta_f32(x, time, alpha, inv_beta, LEVO_DTYPE_SNAKE_PREPARED, y, time, channels, time,
+                                     stream),
+                  detail::kAudio);
+}
+
 // One run_residual / stage node run (src/levo-vae.cpp:90-101), fused.
 inline void fused_unit(const levo_fused_unit &unit, levo_stream_t stream = nullptr) {
     detail::check(levo_vae_fused_unit_f32(&unit, stream), detail::kAudio);

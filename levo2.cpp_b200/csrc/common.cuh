@@ -143,6 +143,17 @@ __device__ __forceinline__ float snake_inv_beta(float beta_log) {
     return __frcp_rn(__fadd_rn(expf(beta_log), 1.0e-9f));
 }
 
+// A channel's alpha and 1/beta from its stored parameter: log form (F32 / F16)
+// or already prepared by levo_snake_params_prepare (LEVO_DTYPE_SNAKE_PREPARED).
+__device__ __forceinline__ float snake_alpha_param(const void *p, int64_t c, int dtype) {
+    const float v = load_param(p, c, dtype);
+    return dtype == LEVO_DTYPE_SNAKE_PREPARED ? v : snake_alpha(v);
+}
+__device__ __forceinline__ float snake_inv_beta_param(const void *p, int64_t c, int dtype) {
+    const float v = load_param(p, c, dtype);
+    return dtype == LEVO_DTYPE_SNAKE_PREPARED ? v : snake_inv_beta(v);
+}
+
 // sin(t)^2, written for this library (no sinf call on the common path):
 //  1. Cody-Waite argument reduction (W. J. Cody, W. Waite, "Software Manual for
 //     the Elementary Functions", 1980): k = rint(t * 2/pi), r = t - k*pi/2 with

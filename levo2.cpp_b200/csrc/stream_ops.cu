@@ -67,8 +67,8 @@ __device__ __forceinline__ ChannelParams channel_params(const StreamArgs &a, con
         if (a.has_bias) p.bias = smem[2 * a.rows + c];
     } else {
         if (SNAKE) {
-            p.alpha = snake_alpha(load_param(a.alog, c, a.pdtype));
-            p.beta = snake_inv_beta(load_param(a.blog, c, a.pdtype));
+            p.alpha = snake_alpha_param(a.alog, c, a.pdtype);
+            p.beta = snake_inv_beta_param(a.blog, c, a.pdtype);
         }
         if (a.has_bias) p.bias = load_param(a.bias, c, a.pdtype);
     }
@@ -168,8 +168,8 @@ __device__ __forceinline__ void stage_params(const StreamArgs &a, float *smem) {
     if (!a.staged) return;
     for (int64_t c = threadIdx.x; c < a.rows; c += blockDim.x) {
         if (SNAKE) {
-            smem[c] = snake_alpha(load_param(a.alog, c, a.pdtype));
-            smem[a.rows + c] = snake_inv_beta(load_param(a.blog, c, a.pdtype));
+            smem[c] = snake_alpha_param(a.alog, c, a.pdtype);
+            smem[a.rows + c] = snake_inv_beta_param(a.blog, c, a.pdtype);
         }
         if (a.has_bias) smem[2 * a.rows + c] = load_param(a.bias, c, a.pdtype);
     }
@@ -304,6 +304,18 @@ int launch_variant(const StreamArgs &a, bool vec, size_t smem_bytes, cudaStream_
     return check_launch(what);
 }
 
+// One thread per channel: alpha = exp(alpha_log), 1/beta, with the kernels' own
+// device arithmetic (snake_alpha / snake_inv_beta), so prepared and log-form
+// launches agree bit for bit.
+__global__ void __launch_bounds__(256) snake_params_kernel(const void *alog, const void *blog, int dtype,
+                                                          int64_t channels, float *alpha, float *inv_beta) {
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < channels;
+         c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        alpha[c] = snake_alpha(load_param(alog, c, dtype));
+        inv_beta[c] = snake_inv_beta(load_param(blog, c, dtype));
+    }
+}
+
 struct StreamRequest {
     const float *u;
     int64_t ldu;
@@ -326,8 +338,8 @@ struct StreamRequest {
 int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
     const std::string w(what);
     if (q.rows < 0 || q.len < 0) return set_error(LEVO_OPS_EINVAL, w + ": negative shape");
-    if (q.pdtype != LEVO_DTYPE_F32 && q.pdtype != LEVO_DTYPE_F16)
-        return set_error(LEVO_OPS_EINVAL, w + ": parameter dtype must be F32 or F16");
+    if (q.pdtype != LEVO_DTYPE_F32 && q.pdtype != LEVO_DTYPE_F16 && q.pdtype != LEVO_DTYPE_SNAKE_PREPARED)
+        return set_error(LEVO_OPS_EINVAL, w + ": parameter dtype must be F32, F16 or SNAKE_PREPARED");
     if (q.rows == 0 || q.len == 0) return LEVO_OPS_OK;  // empty tensors: nothing to read or write
     if (q.u == nullptr) return set_error(LEVO_OPS_EINVAL, w + ": input is null");
     if (q.need_snake && (q.alog == nullptr || q.blog == nullptr))
@@ -434,6 +446,28 @@ int fused_unit(const levo_fused_unit &unit, cudaStream_t stream) {
 }  // namespace levo
 
 extern "C" {
+
+LEVO_OPS_API int levo_snake_params_prepare(const void *alpha_log, const void *beta_log, int param_dtype,
+                                           int64_t channels, float *alpha_out, float *inv_beta_out,
+                                           levo_stream_t stream) {
+    using namespace levo;
+    clear_error();
+    const std::string w = "levo_snake_params_prepare";
+    if (param_dtype != LEVO_DTYPE_F32 && param_dtype != LEVO_DTYPE_F16)
+        return set_error(LEVO_OPS_EINVAL, w + ": parameter dtype must be F32 or F16");
+    if (channels < 0) return set_error(LEVO_OPS_EINVAL, w + ": negative channel count");
+    if (channels == 0) return LEVO_OPS_OK;
+    if (!alpha_log || !beta_log || !alpha_out || !inv_beta_out)
+        return set_error(LEVO_OPS_EINVAL, w + ": required pointer is null");
+    const size_t pbytes = param_dtype == LEVO_DTYPE_F16 ? 2 : 4;
+    if (!aligned_to(alpha_log, pbytes) || !aligned_to(beta_log, pbytes) || !aligned_to(alpha_out, 4) ||
+        !aligned_to(inv_beta_out, 4))
+        return set_error(LEVO_OPS_EINVAL, w + ": pointer is not aligned to its element size");
+    const int64_t grid = std::min<int64_t>((channels + 255) / 256, static_cast<int64_t>(sm_count()) * 4);
+    snake_params_kernel<<<static_cast<unsigned>(grid), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        alpha_log, beta_log, param_dtype, channels, alpha_out, inv_beta_out);
+    return check_launch(w.c_str());
+}
 
 LEVO_OPS_API int levo_snakebeta_f32(const float *x, int64_t ldx, const void *alpha_log,
                                     const void *beta_log, int param_dtype, float *y, int64_t ldy,

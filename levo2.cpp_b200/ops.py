@@ -18,7 +18,7 @@ from typing import Optional
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblevo_b200.so"
 
 OK, EINVAL, ELAUNCH, EUNSUPPORTED, ENONFINITE, ECANCELLED, ENOMEM, ECUDA = 0, -1, -2, -3, -4, -5, -6, -7
-DTYPE_F32, DTYPE_F16 = 0, 1
+DTYPE_F32, DTYPE_F16, DTYPE_SNAKE_PREPARED = 0, 1, 2
 FUSED_TANH = 1
 NORM_F16_BOUNDARY = 1
 CHAIN_TANH, CHAIN_TIMING = 1, 2
@@ -120,6 +120,7 @@ _INT = ctypes.c_int
 SIGNATURES = {
     "levo_ops_abi_version": (_U32, []),
     "levo_ops_last_error": (ctypes.c_char_p, []),
+    "levo_snake_params_prepare": (_INT, [_P, _P, _INT, _I64, _P, _P, _P]),
     "levo_snakebeta_f32": (_INT, [_P, _I64, _P, _P, _INT, _P, _I64, _I64, _I64, _P]),
     "levo_channel_bias_add_f32": (_INT, [_P, _P, _INT, _P, _I64, _I64, _P]),
     "levo_vae_fused_unit_f32": (_INT, [ctypes.POINTER(FusedUnit), _P]),
@@ -213,8 +214,24 @@ def _pdtype(t) -> int:
     raise ValueError("parameters must be float32 or float16")
 
 
-def snakebeta_t(x, alpha_log, beta_log, out=None):
-    """y = x + sin(x*exp(alpha_log))^2 / (exp(beta_log)+1e-9) over [C, T] (row stride honoured)."""
+def snake_params_prepare_t(alpha_log, beta_log):
+    """Returns (alpha, inv_beta) F32 [channels]: exp(alpha_log) and 1/(exp(beta_log)+1e-9),
+    for snakebeta_t(..., prepared=True) and fused units with DTYPE_SNAKE_PREPARED."""
+    import torch
+
+    _require_cuda(alpha_log, beta_log)
+    if alpha_log.dtype != beta_log.dtype or alpha_log.numel() != beta_log.numel():
+        raise ValueError("alpha_log and beta_log must share a dtype and a channel count")
+    alpha = torch.empty(alpha_log.numel(), dtype=torch.float32, device=alpha_log.device)
+    inv_beta = torch.empty_like(alpha)
+    check(lib().levo_snake_params_prepare(_ptr(alpha_log), _ptr(beta_log), _pdtype(alpha_log), alpha_log.numel(),
+                                          _ptr(alpha), _ptr(inv_beta), _stream(alpha_log.device)))
+    return alpha, inv_beta
+
+
+def snakebeta_t(x, alpha_log, beta_log, out=None, prepared=False):
+    """y = x + sin(x*exp(alpha_log))^2 / (exp(beta_log)+1e-9) over [C, T] (row stride honoured).
+    With prepared=True the parameters are snake_params_prepare_t's (alpha, inv_beta)."""
     import torch
 
     _require_cuda(x, alpha_log, beta_log)
@@ -224,8 +241,11 @@ def snakebeta_t(x, alpha_log, beta_log, out=None):
         raise ValueError("alpha_log and beta_log must share a dtype")
     if alpha_log.numel() != x.shape[0] or beta_log.numel() != x.shape[0]:
         raise ValueError("SnakeBeta parameters must have shape [1, channels, 1]")
+    if prepared and alpha_log.dtype != torch.float32:
+        raise ValueError("prepared SnakeBeta parameters are float32")
     y = torch.empty_like(x, memory_format=torch.contiguous_format) if out is None else out
-    check(lib().levo_snakebeta_f32(_ptr(x), x.stride(0), _ptr(alpha_log), _ptr(beta_log), _pdtype(alpha_log),
+    pdtype = DTYPE_SNAKE_PREPARED if prepared else _pdtype(alpha_log)
+    check(lib().levo_snakebeta_f32(_ptr(x), x.stride(0), _ptr(alpha_log), _ptr(beta_log), pdtype,
                                    _ptr(y), y.stride(0), x.shape[0], x.shape[1], _stream(x.device)))
     return y
 

@@ -50,6 +50,13 @@ int main() {
             CHECK(std::fabs(y[c * 3 + t] - (v + s * s / (std::exp(b[c]) + 1.0e-9F))) < 2.0e-5F);
         }
 
+    // Prepared parameters give the same bits.
+    float *dal = to_device(std::vector<float>(2)), *dib = to_device(std::vector<float>(2));
+    float *dy2 = to_device(std::vector<float>(6));
+    snake_params_prepare(da, db, dal, dib, 2);
+    snake_beta_prepared(dx, dal, dib, dy2, 2, 3);
+    CHECK(to_host(dy2, 6) == y);
+
     // Errors keep the reference's exception types and prefixes.
     bool thrown = false;
     try {

@@ -87,6 +87,18 @@ def test_invalid_arguments_are_einval_without_gpu(ops):
     assert lib.levo_vae_fused_unit_f32(ctypes.byref(u), None) == ops.EINVAL
 
 
+def test_snake_params_prepare_validation_without_gpu(ops):
+    lib = ops.lib()
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.addressof(buf)
+    assert lib.levo_snake_params_prepare(p, p, ops.DTYPE_SNAKE_PREPARED, 4, p, p, None) == ops.EINVAL
+    assert lib.levo_snake_params_prepare(p, None, 0, 4, p, p, None) == ops.EINVAL
+    assert "null" in ops.last_error()
+    assert lib.levo_snake_params_prepare(p, p, 0, -1, p, p, None) == ops.EINVAL
+    assert lib.levo_snake_params_prepare(p + 2, p, 0, 4, p, p, None) == ops.EINVAL
+    assert lib.levo_snakebeta_f32(p, 4, p, p, 3, p, 4, 1, 4, None) == ops.EINVAL  # unknown dtype
+
+
 def test_zero_sizes_are_noops_without_gpu(ops):
     lib = ops.lib()
     buf = (ctypes.c_float * 8)()
@@ -95,6 +107,7 @@ def test_zero_sizes_are_noops_without_gpu(ops):
     assert lib.levo_snakebeta_f32(p, 0, p, p, 0, p, 0, 5, 0, None) == ops.OK
     assert lib.levo_add_layernorm_f32(p, None, p, p, None, p, 0, 16, 1e-5, 0, None) == ops.OK
     assert lib.levo_weightnorm_f32(p, p, p, None, 0, 7, None) == ops.OK
+    assert lib.levo_snake_params_prepare(p, p, 0, 0, p, p, None) == ops.OK
 
 
 def test_chain_rejects_bad_topology_without_gpu(ops):

@@ -177,3 +177,43 @@ def test_fused_unit_in_place_like_the_chain(ops, orc, dev):
     xw, yw = orc.fused_unit(u, b, r, a, bl)
     assert np.array_equal(tr.cpu().numpy(), xw)
     assert_close(tu.cpu().numpy(), yw, TOL)
+
+
+@pytest.mark.parametrize("pdt", [torch.float32, torch.float16])
+def test_snake_params_prepare(ops, dev, pdt):
+    rng = np.random.default_rng(41)
+    a, b = _params(rng, 5000, scale=2.0)
+    ta, tb = torch.from_numpy(a).to(dev, pdt), torch.from_numpy(b).to(dev, pdt)
+    alpha, inv_beta = ops.snake_params_prepare_t(ta, tb)
+    a64, b64 = ta.double().cpu().numpy(), tb.double().cpu().numpy()
+    # expf is within 2 ulp; the reciprocal is IEEE-rounded
+    np.testing.assert_allclose(alpha.cpu().numpy(), np.exp(a64), rtol=3e-7, atol=0)
+    np.testing.assert_allclose(inv_beta.cpu().numpy(), 1.0 / (np.exp(b64) + 1e-9), rtol=5e-7, atol=0)
+
+
+@pytest.mark.parametrize("shape", [(1, 7), (16, 1001), (128, 4096), (3000, 9), (64, 20008), (5000, 8)])
+@pytest.mark.parametrize("pdt", [torch.float32, torch.float16])
+def test_snakebeta_prepared_equals_log_form(ops, dev, shape, pdt):
+    """Every dispatch form (rows, flat vectors, scalar, staged or not) gives the same bits."""
+    rng = np.random.default_rng(sum(shape))
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(dev)
+    a, b = [torch.from_numpy(p).to(dev, pdt) for p in _params(rng, shape[0])]
+    alpha, inv_beta = ops.snake_params_prepare_t(a, b)
+    want = ops.snakebeta_t(x, a, b)
+    got = ops.snakebeta_t(x, alpha, inv_beta, prepared=True)
+    assert torch.equal(got, want)
+    xs = x[:, 1:]  # strided view: scalar path
+    assert torch.equal(ops.snakebeta_t(xs, alpha, inv_beta, prepared=True), ops.snakebeta_t(xs, a, b))
+
+
+def test_fused_unit_prepared_params(ops, dev):
+    rng = np.random.default_rng(43)
+    c, t = 40, 8008
+    u, r = (torch.from_numpy(v).to(dev) for v in rng.standard_normal((2, c, t)).astype(np.float32))
+    bias = torch.from_numpy((0.02 * rng.standard_normal(c)).astype(np.float32)).to(dev)
+    a, b = (torch.from_numpy(p).to(dev) for p in _params(rng, c))
+    alpha, inv_beta = ops.snake_params_prepare_t(a, b)
+    out = [torch.empty_like(u) for _ in range(4)]
+    ops.fused_unit_t(u, bias, r, a, b, out[0], out[1])
+    ops.fused_unit_t(u, bias, r, alpha, inv_beta, out[2], out[3], param_dtype=ops.DTYPE_SNAKE_PREPARED)
+    assert torch.equal(out[0], out[2]) and torch.equal(out[1], out[3])
