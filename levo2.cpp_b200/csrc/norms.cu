@@ -317,6 +317,21 @@ struct Chunk<__half> {
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
+    // x + r rounded to F16 in one HADD2 per pair.  The F32 sum of two F16
+    // values rounded to F16 is the same number: F32 carries 24 >= 2*11 + 1
+    // significand bits, so the double rounding is innocuous (S. A. Figueroa,
+    // "When is double rounding innocuous?", SIGNUM Newsletter 30(3), 1995).
+    __device__ static uint4 add(const uint4 &a, const uint4 &b) {
+        const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 s = __hadd2(*reinterpret_cast<const __half2 *>(&wa[i]),
+                                      *reinterpret_cast<const __half2 *>(&wb[i]));
+            w[i] = *reinterpret_cast<const uint32_t *>(&s);
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
 };
 template <>
 struct Chunk<float> {
@@ -330,6 +345,12 @@ struct Chunk<float> {
     __device__ static uint4 pack(const float *v) {
         return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
                           __float_as_uint(v[3]));
+    }
+    __device__ static uint4 add(const uint4 &a, const uint4 &b) {
+        return make_uint4(__float_as_uint(__fadd_rn(__uint_as_float(a.x), __uint_as_float(b.x))),
+                          __float_as_uint(__fadd_rn(__uint_as_float(a.y), __uint_as_float(b.y))),
+                          __float_as_uint(__fadd_rn(__uint_as_float(a.z), __uint_as_float(b.z))),
+                          __float_as_uint(__fadd_rn(__uint_as_float(a.w), __uint_as_float(b.w))));
     }
 };
 
@@ -375,8 +396,17 @@ __global__ void __launch_bounds__(kStagedRows * 32) add_norm_staged_kernel(const
         float sum = 0.f;
         for (int i = lane; i < chunks; i += 32) {
             float h[N];
-            Chunk<T>::unpack(xs[i], h);
             const bool gated = MOD && a.gate;
+            if (!gated && rg) {
+                // plain residual add, in the activation type
+                const uint4 hc = Chunk<T>::add(xs[i], rs[i]);
+                xs[i] = hc;
+                Chunk<T>::unpack(hc, h);
+#pragma unroll
+                for (int j = 0; j < N; ++j) sum += LAYER ? h[j] : h[j] * h[j];
+                continue;
+            }
+            Chunk<T>::unpack(xs[i], h);
             if (gated) {
                 float g[N];
                 load_cols<N>(a.gate + mod_off + i * N, g);

@@ -4,14 +4,14 @@
 // Each is a single HBM pass: every input element is read once with a 256-bit
 // load and every output written once with a 256-bit store.  Two vector forms:
 //  * rows form (rows of a multiple of 8 values, 32-byte aligned tensors, the
-//    decoder's case): the tensor is cut into row chunks of kThreads*UNROLL
-//    vectors; each CTA of the persistent grid walks one contiguous range of
-//    chunks, so the channel is uniform per chunk and its parameters (alpha,
-//    1/beta, bias: promoted to F32 and exponentiated) are recomputed in
-//    registers only when the range crosses into the next row.
-//  * flat form (any row length, any common 32-byte phase): the flat element
-//    space is walked in tiles with parameters staged in shared memory once per
-//    CTA; a vector that straddles a row boundary selects them per element.
+//    decoder's case): the tensor is cut into row chunks of kRowThreads*UNROLL
+//    vectors and a grid far larger than the resident CTA count walks them, so
+//    the channel is uniform per chunk and its parameters (alpha, 1/beta, bias:
+//    promoted to F32 and exponentiated) are computed in registers per chunk.
+//  * flat form (any row length, any common 32-byte phase): one CTA per tile of
+//    the flat element space; parameters are cached per thread by channel (or
+//    staged in shared memory when there are few channels), and a vector that
+//    straddles a row boundary selects them per element.
 // A scalar form covers strided rows and mismatched alignments.
 #include <algorithm>
 #include <cmath>
@@ -23,10 +23,16 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 2;
-// Rows form: 128-thread CTAs, one vector per thread per chunk for the 2-input
-// residual unit and two for the 1-input units (the fastest shape in a sweep of
-// block size 128-512 and unroll 1-8 on the config-4 chain).
+// Rows form: 128-thread CTAs.  Measured on the config-4 chain (sweep of block
+// size 128-256, unroll 1-8 and grid size) on B200:
+//  * 1-input units (SnakeBeta, post / upsample units): four vectors per thread
+//    per chunk and one CTA per chunk (~6.0-6.5 TB/s; a grid of resident CTAs
+//    walking chunk ranges reached ~5.2-5.5);
+//  * 2-input residual unit: one vector per thread per chunk and a grid of 16x
+//    the resident CTAs, each walking a short chunk range (6.18 TB/s; 5.88 with
+//    one CTA per chunk, 5.90 with 1x).
 constexpr int kRowThreads = 128;
+constexpr int kResidualGridPerResident = 16;
 constexpr int64_t kMaxStagedChannels = 4096;
 
 struct StreamArgs {
@@ -109,7 +115,11 @@ __device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelPar
 }
 
 // Rows form: CTA b owns chunks [b*chunks/G, (b+1)*chunks/G); chunk q covers
-// vectors [k*kThreads*UNROLL, (k+1)*kThreads*UNROLL) of row c, q = c*cpr + k.
+// vectors [k*kRowThreads*UNROLL, (k+1)*kRowThreads*UNROLL) of row c, q = c*cpr + k.
+// Short-lived CTAs that the block scheduler refills keep HBM busier than a
+// persistent grid (a plain 2-in/2-out stream on B200: ~6.8 against ~6.0 TB/s),
+// so G is far above the resident CTA count (launch_rows).  The loads of a
+// chunk are issued before its channel parameters are computed.
 template <bool HAS_RES, bool SNAKE, int UNROLL>
 __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamArgs a) {
     pdl_wait();
@@ -119,7 +129,6 @@ __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamAr
     if (q0 >= q1) return;
     int64_t c = row_of(q0, a.chunks_per_row, a.inv_chunks_per_row);
     int64_t k = q0 - c * a.chunks_per_row;
-    ChannelParams p = channel_params<SNAKE>(a, nullptr, c);
     for (int64_t q = q0; q < q1; ++q) {
         const size_t row = static_cast<size_t>(c) * a.len;
         const int64_t v0 = k * (kRowThreads * UNROLL) + threadIdx.x;
@@ -132,6 +141,7 @@ __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamAr
                 if (HAS_RES) rr[j] = ld8(a.res + row + v * 8);
             }
         }
+        const ChannelParams p = channel_params<SNAKE>(a, nullptr, c);
 #pragma unroll
         for (int j = 0; j < UNROLL; ++j) {
             const int64_t v = v0 + j * kRowThreads;
@@ -141,10 +151,9 @@ __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamAr
             if (a.write_x) st8(a.x_out + row + v * 8, xo);
             if (a.write_y) st8(a.y_out + row + v * 8, yo);
         }
-        if (++k == a.chunks_per_row && q + 1 < q1) {
+        if (++k == a.chunks_per_row) {
             k = 0;
             ++c;
-            p = channel_params<SNAKE>(a, nullptr, c);
         }
     }
 }
@@ -267,18 +276,27 @@ __global__ void __launch_bounds__(kThreads) stream_scalar_kernel(const StreamArg
 
 template <bool HAS_RES, bool SNAKE>
 int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
-    constexpr int kRowUnroll = HAS_RES ? 1 : 2;
+    constexpr int kRowUnroll = HAS_RES ? 1 : 4;
     auto kernel = stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll>;
     a.staged = 0;
     a.vec_per_row = a.len / 8;
     a.chunks_per_row = (a.vec_per_row + kRowThreads * kRowUnroll - 1) / (kRowThreads * kRowUnroll);
     a.chunks = a.rows * a.chunks_per_row;
     a.inv_chunks_per_row = 1.0 / static_cast<double>(a.chunks_per_row);
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kRowThreads, 0) != cudaSuccess ||
-        per_sm <= 0)
-        per_sm = 1;
-    const int64_t grid = std::min<int64_t>(a.chunks, static_cast<int64_t>(sm_count()) * per_sm);
+    // 1-input units: one CTA per chunk (past 2^31 - 1 chunks a CTA takes a
+    // contiguous range); residual unit: 16x the resident CTAs.
+    int64_t cap = 0x7fffffff;
+    if (HAS_RES) {
+        // resident CTAs per SM: a property of the kernel and the architecture, queried once
+        static const int per_sm = [kernel] {
+            int n = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kRowThreads, 0) != cudaSuccess || n <= 0)
+                n = 1;
+            return n;
+        }();
+        cap = static_cast<int64_t>(sm_count()) * per_sm * kResidualGridPerResident;
+    }
+    const int64_t grid = std::min<int64_t>(a.chunks, cap);
     const cudaError_t err = launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kRowThreads), 0, stream, a);
     if (err != cudaSuccess)
         return set_error(LEVO_OPS_ELAUNCH, std::string(what) + ": kernel launch failed: " + cudaGetErrorString(err));
@@ -296,7 +314,9 @@ int launch_variant(const StreamArgs &a, bool vec, size_t smem_bytes, cudaStream_
         per_sm = 1;
     const int64_t work_items = vec ? (a.nvec + kUnroll - 1) / kUnroll : a.n;
     const int64_t needed = std::max<int64_t>(1, (work_items + kThreads - 1) / kThreads);
-    const int64_t grid = std::min<int64_t>(needed, static_cast<int64_t>(sm_count()) * per_sm);
+    // vector form: one CTA per tile, as in the rows form; scalar form: persistent grid
+    const int64_t grid = vec ? std::min<int64_t>(needed, 0x7fffffff)
+                             : std::min<int64_t>(needed, static_cast<int64_t>(sm_count()) * per_sm);
     const cudaError_t err =
         launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem_bytes, stream, a);
     if (err != cudaSuccess)
@@ -403,10 +423,12 @@ int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
     }
 
     // Stage the per-channel parameters in shared memory only when each CTA has
-    // enough elements to amortise exponentiating all of them (the stage-0 entry
-    // unit, 2048 channels x 750 frames, computes them per vector instead).
+    // enough elements to amortise exponentiating all of them (a vector-form CTA
+    // holds one tile of kThreads*kUnroll*8 values; the stage-0 entry unit, 2048
+    // channels, computes them per vector instead).
     const int nparams = (snake ? 2 : 0) + (a.has_bias ? 1 : 0);
-    const int64_t per_cta = a.n / (static_cast<int64_t>(sm_count()) * 8);
+    const int64_t per_cta = vec ? static_cast<int64_t>(kThreads) * kUnroll * 8
+                                : a.n / (static_cast<int64_t>(sm_count()) * 8);
     a.staged = nparams > 0 && q.rows <= kMaxStagedChannels && q.rows * 64 <= per_cta;
     const size_t smem_bytes = a.staged ? static_cast<size_t>(3 * q.rows) * sizeof(float) : 0;
 

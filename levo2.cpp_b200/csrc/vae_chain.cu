@@ -563,7 +563,8 @@ LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int
     if (n == 0) return LEVO_OPS_OK;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (out_length % 8 == 0 && aligned_to(out, 32)) {
-        const int64_t grid = std::min<int64_t>((n / 8 + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
+        // one vector per thread, one CTA per 256 vectors (short-lived CTAs stream best)
+        const int64_t grid = std::min<int64_t>((n / 8 + 255) / 256, 0x7fffffff);
         const cudaError_t err =
             launch_pdl(conv_standin_vec8_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, s, in,
                        in_channels, in_length, out, out_channels, out_length, stride,
