@@ -44,7 +44,7 @@ typedef enum {
     LEVO_OPS_EINVAL = -1,       /* bad argument: null pointer, bad shape, misaligned pointer */
     LEVO_OPS_ELAUNCH = -2,      /* a kernel launch failed (cudaGetLastError) */
     LEVO_OPS_EUNSUPPORTED = -3, /* valid request outside what this build implements */
-    LEVO_OPS_ENONFINITE = -4,   /* a finiteness check failed (Euler state / velocity) */
+    LEVO_OPS_ENONFINITE = -4,   /* a finiteness check failed (Euler state / velocity, VAE latent) */
     LEVO_OPS_ECANCELLED = -5,   /* the cancel callback asked to stop between windows */
     LEVO_OPS_ENOMEM = -6,       /* device or pinned host allocation failed (chain create) */
     LEVO_OPS_ECUDA = -7         /* any other CUDA runtime error */
@@ -242,12 +242,29 @@ LEVO_OPS_API int levo_vae_chain_decode(levo_vae_chain *chain, const float *laten
                                        float *audio, uint32_t flags, levo_stream_t stream);
 
 /*
+ * Stage capture, vae_decoder::decode's capture_stages (src/levo-vae.cpp:230-231,
+ * 271-274): after this call every decode also writes each stage's output
+ * x_s [stage_width[s]][frames * prod(strides[0..s])] (the hidden state after
+ * the stage's last residual unit, channel-major F32) to stage_out[s].
+ * Destinations may be host or device memory (the copies use unified
+ * addressing); they must hold the largest frame count decoded.  count must be
+ * n_stages; stage_out == NULL or count == 0 turns capture off.  While capture
+ * is on, levo_vae_chain_decode_windows takes one window at a time.  Each
+ * stage then stores x once more (4 B/elem) and copies it out.
+ */
+LEVO_OPS_API int levo_vae_chain_set_stage_capture(levo_vae_chain *chain, float *const *stage_out,
+                                                  int32_t count);
+
+/*
  * Host-to-host decode of `windows` independent windows: latents_host
  * [windows][latent_dim][frames] -> audio_host [windows][audio_channels][samples].
  * Copies in and out inside the call (pinned host buffers overlap the copies
  * with the next window's kernels), polls `cancel` before each window as the
  * reference DECODE loop does (src/cantor-abi.cpp:901-913,
  * src/levo-render.cpp:442-451) and returns LEVO_OPS_ECANCELLED when it fires.
+ * Like vae_decoder::decode (src/levo-vae.cpp:189-191) it rejects a window
+ * whose latent holds a non-finite value, before that window's work, with
+ * LEVO_OPS_ENONFINITE ("latent payload contains a non-finite value").
  * Synchronous: returns after the last window's audio is in host memory.
  */
 LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const float *latents_host,

@@ -14,7 +14,9 @@
 #ifndef LEVO_OPS_HPP
 #define LEVO_OPS_HPP
 
+#include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -142,6 +144,14 @@ void solve_flow_euler(const euler_device_input &in, int64_t steps, bool cfg, flo
                   detail::kFlow);
 }
 
+// vae_decode_result (src/levo-vae.h:13-19).
+struct vae_decode_result {
+    std::size_t frames = 0;
+    std::size_t samples_per_channel = 0;
+    std::vector<float> audio;                       // planar [audio_channels][samples_per_channel]
+    std::vector<std::vector<float>> stage_outputs;  // capture_stages: stage s as [stage_width[s]][L_s]
+};
+
 // vae_decoder (src/levo-vae.h:21-43) over the elementwise chain.
 class vae_decoder {
    public:
@@ -155,24 +165,51 @@ class vae_decoder {
         topology_ = topology;
     }
 
-    // Host latent [latent_dim][frames] -> host audio [audio_channels][frames * prod(strides)],
-    // like vae_decoder::decode (src/levo-vae.cpp:172-276).
-    std::vector<float> decode(const std::vector<float> &latent, int64_t frames, bool tanh = false,
-                              levo_stream_t stream = nullptr) const {
-        int64_t up = 1;
-        for (int s = 0; s < topology_.n_stages; ++s) up *= topology_.stage_stride[s];
-        if (frames <= 0 || static_cast<int64_t>(latent.size()) != frames * topology_.latent_dim)
+    // vae_decoder::decode (src/levo-vae.cpp:172-276): host latent [latent_dim][frames] -> host audio
+    // [audio_channels][frames * prod(strides)].  capture_stages also returns every stage's output;
+    // `cancelled` is polled before the work and after it, as the reference polls around its graph
+    // (src/levo-vae.cpp:248-255).  `tanh` is the BASELINE epilogue (the reference has none).
+    vae_decode_result decode(const std::vector<float> &latent, std::size_t frames, bool capture_stages = false,
+                             const std::function<bool()> &cancelled = {}, bool tanh = false,
+                             levo_stream_t stream = nullptr) const {
+        if (frames == 0 || latent.size() != frames * static_cast<std::size_t>(topology_.latent_dim))
             throw std::runtime_error("LeVo VAE: latent payload does not have shape [64,frames]");
-        std::vector<float> audio(static_cast<size_t>(topology_.audio_channels * frames * up));
-        detail::check(levo_vae_chain_decode_windows(chain_.get(), latent.data(), 1, frames, audio.data(),
-                                                    tanh ? LEVO_CHAIN_TANH : 0u, nullptr, nullptr, stream),
+        vae_decode_result result;
+        result.frames = frames;
+        std::size_t length = frames;
+        if (capture_stages) result.stage_outputs.resize(static_cast<std::size_t>(topology_.n_stages));
+        std::vector<float *> dest;
+        for (int s = 0; s < topology_.n_stages; ++s) {
+            length *= static_cast<std::size_t>(topology_.stage_stride[s]);
+            if (capture_stages) {
+                auto &stage = result.stage_outputs[static_cast<std::size_t>(s)];
+                stage.resize(static_cast<std::size_t>(topology_.stage_width[s]) * length);
+                dest.push_back(stage.data());
+            }
+        }
+        result.samples_per_channel = length;
+        result.audio.resize(static_cast<std::size_t>(topology_.audio_channels) * length);
+        struct capture_scope {  // capture stays on for this call only
+            levo_vae_chain *chain;
+            ~capture_scope() { levo_vae_chain_set_stage_capture(chain, nullptr, 0); }
+        } scope{chain_.get()};
+        if (capture_stages)
+            detail::check(levo_vae_chain_set_stage_capture(chain_.get(), dest.data(), topology_.n_stages),
+                          detail::kVae);
+        const levo_cancel_fn poll = cancelled ? &poll_cancel : nullptr;
+        void *user = cancelled ? const_cast<std::function<bool()> *>(&cancelled) : nullptr;
+        detail::check(levo_vae_chain_decode_windows(chain_.get(), latent.data(), 1, static_cast<int64_t>(frames),
+                                                    result.audio.data(), tanh ? LEVO_CHAIN_TANH : 0u, poll, user,
+                                                    stream),
                       detail::kVae);
-        return audio;
+        if (cancelled && cancelled()) throw operation_cancelled();
+        return result;
     }
 
     levo_vae_chain *handle() const noexcept { return chain_.get(); }
 
    private:
+    static int poll_cancel(void *user) { return (*static_cast<std::function<bool()> *>(user))() ? 1 : 0; }
     struct deleter {
         void operator()(levo_vae_chain *c) const noexcept { levo_vae_chain_destroy(c); }
     };

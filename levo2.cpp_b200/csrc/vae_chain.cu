@@ -210,6 +210,9 @@ struct levo_vae_chain {
     cudaEvent_t copied[2] = {nullptr, nullptr};
     levo_conv_fn conv = nullptr;
     void *conv_user = nullptr;
+    // stage capture (levo_vae_chain_set_stage_capture): per-stage destinations, host or device
+    float *capture[LEVO_VAE_MAX_STAGES] = {};
+    int32_t n_capture = 0;
     // timing
     std::vector<cudaEvent_t> events;
     int next_event = 0;
@@ -325,6 +328,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
     const char *base = static_cast<const char *>(c->params);
     auto P = [&](int64_t off) -> const void * { return base + off * esize; };
     const bool timing = (flags & LEVO_CHAIN_TIMING) != 0;
+    const bool capturing = c->n_capture > 0;
     auto snake_of = [&](int stage, int unit) -> SnakeRef {
         // Activation applied before conv `unit` of `stage`; unit == n_residual
         // means the next stage's upsample activation (or the output one).
@@ -396,7 +400,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
             u.bias = P(so.up_bias);
             u.alpha_log = sn.alpha;
             u.beta_log = sn.beta;
-            u.x_out = t.n_residual > 0 ? c->X : nullptr;
+            u.x_out = (t.n_residual > 0 || capturing) ? c->X : nullptr;
             u.y_out = cur;
             u.channels = cout;
             u.time = lout;
@@ -460,7 +464,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
                 u.residual = c->X;
                 u.alpha_log = sn.alpha;
                 u.beta_log = sn.beta;
-                u.x_out = r + 1 < t.n_residual ? c->X : nullptr;
+                u.x_out = (r + 1 < t.n_residual || capturing) ? c->X : nullptr;
                 u.y_out = cur;
                 u.channels = cout;
                 u.time = lout;
@@ -468,6 +472,13 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
                 rc = run_unit(c, timing, LEVO_KCLASS_RESIDUAL, u, s);
                 if (rc != LEVO_OPS_OK) return rc;
             }
+        }
+        if (capturing) {
+            // the stage output (src/levo-vae.cpp:230-231) is x, now in X
+            const cudaError_t err = cudaMemcpyAsync(c->capture[st], c->X,
+                                                    static_cast<size_t>(cout * lout) * sizeof(float),
+                                                    cudaMemcpyDefault, s);
+            if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain: stage capture copy");
         }
         cin = cout;
         len = lout;
@@ -673,6 +684,26 @@ LEVO_OPS_API void levo_vae_chain_destroy(levo_vae_chain *chain) {
     levo::free_chain(chain);
 }
 
+LEVO_OPS_API int levo_vae_chain_set_stage_capture(levo_vae_chain *chain, float *const *stage_out,
+                                                  int32_t count) {
+    using namespace levo;
+    clear_error();
+    if (chain == nullptr) return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_set_stage_capture: chain is null");
+    if (stage_out == nullptr || count == 0) {
+        chain->n_capture = 0;
+        return LEVO_OPS_OK;
+    }
+    if (count != chain->topo.n_stages)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_set_stage_capture: one destination per stage is required");
+    for (int32_t i = 0; i < count; ++i)
+        if (stage_out[i] == nullptr || !aligned_to(stage_out[i], 4))
+            return set_error(LEVO_OPS_EINVAL,
+                             "levo_vae_chain_set_stage_capture: stage destination is null or not 4-byte aligned");
+    for (int32_t i = 0; i < count; ++i) chain->capture[i] = stage_out[i];
+    chain->n_capture = count;
+    return LEVO_OPS_OK;
+}
+
 LEVO_OPS_API int levo_vae_chain_decode(levo_vae_chain *chain, const float *latent, int64_t frames,
                                        float *audio, uint32_t flags, levo_stream_t stream) {
     using namespace levo;
@@ -697,6 +728,8 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
     if (rc != LEVO_OPS_OK) return rc;
     if (latents_host == nullptr || audio_host == nullptr || windows < 0)
         return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_decode_windows: invalid host buffers or window count");
+    if (chain->n_capture > 0 && windows > 1)
+        return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_decode_windows: stage capture holds one window");
     DeviceGuard guard(chain->device);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const levo_vae_topology &t = chain->topo;
@@ -711,11 +744,21 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
             return set_error(LEVO_OPS_ECANCELLED,
                              "levo_vae_chain_decode_windows: cancelled before window " + std::to_string(w));
         }
+        // vae_decoder::decode rejects non-finite latents before any work (src/levo-vae.cpp:189-191)
+        const float *lat_w = latents_host + w * lat_elems;
+        for (int64_t i = 0; i < lat_elems; ++i) {
+            if (!std::isfinite(lat_w[i])) {
+                cudaStreamSynchronize(s);
+                cudaStreamSynchronize(chain->copy_stream);
+                return set_error(LEVO_OPS_ENONFINITE, "levo_vae_chain_decode_windows: latent payload contains a "
+                                                      "non-finite value (window " + std::to_string(w) + ")");
+            }
+        }
         const int slot = static_cast<int>(w & 1);
         // The slot's previous audio must have left the device before reuse.
         if (pending[slot]) err = cudaStreamWaitEvent(s, chain->copied[slot], 0);
         if (err == cudaSuccess)
-            err = cudaMemcpyAsync(chain->lat[slot], latents_host + w * lat_elems,
+            err = cudaMemcpyAsync(chain->lat[slot], lat_w,
                                   static_cast<size_t>(lat_elems) * sizeof(float), cudaMemcpyHostToDevice, s);
         if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: latent upload");
         rc = decode_one(chain, chain->lat[slot], frames, chain->audio[slot], flags, s);

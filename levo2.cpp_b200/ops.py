@@ -129,6 +129,7 @@ SIGNATURES = {
     "levo_vae_chain_create": (_INT, [ctypes.POINTER(_P), ctypes.POINTER(Topology), _P, _I64, CONV_FN, _P, _INT]),
     "levo_vae_chain_create_f16": (_INT, [ctypes.POINTER(_P), ctypes.POINTER(Topology), _P, _I64, CONV_FN, _P, _INT]),
     "levo_vae_chain_destroy": (None, [_P]),
+    "levo_vae_chain_set_stage_capture": (_INT, [_P, _P, _I32]),
     "levo_vae_chain_decode": (_INT, [_P, _P, _I64, _P, _U32, _P]),
     "levo_vae_chain_decode_windows": (_INT, [_P, _P, _I64, _I64, _P, _U32, CANCEL_FN, _P, _P]),
     "levo_vae_chain_timing": (_INT, [_P, ctypes.POINTER(KernelTiming), _INT]),
@@ -492,6 +493,18 @@ class VaeChain:
             stream = torch.cuda.current_stream(self.device).cuda_stream
         check(lib().levo_vae_chain_decode_windows(self.handle, lat_ptr, windows, frames, out_ptr, flags, cb, None,
                                                   stream))
+
+    def set_stage_capture(self, stage_out) -> None:
+        """stage_out: one F32 buffer per stage (CUDA tensors or host arrays, [width_s, L_s] for the
+        frames decoded), or None to stop capturing.  The buffers must outlive the decodes."""
+        if stage_out is None:
+            self._capture = None
+            check(lib().levo_vae_chain_set_stage_capture(self.handle, None, 0))
+            return
+        ptrs = [o.ctypes.data if hasattr(o, "ctypes") else o.data_ptr() for o in stage_out]
+        arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+        check(lib().levo_vae_chain_set_stage_capture(self.handle, ctypes.cast(arr, ctypes.c_void_p), len(ptrs)))
+        self._capture = list(stage_out)  # keep the buffers alive
 
     def timing(self, reset: bool = True) -> dict:
         arr = (KernelTiming * len(KCLASS_NAMES))()

@@ -240,6 +240,13 @@ void oracle_conv_standin_f32(const float *in, int64_t cin, int64_t lin, float *o
  * separate add node (src/levo-audio-ops.cpp:74-87). */
 int oracle_vae_chain_f32(const int32_t *topo, const float *P, const float *latent, int64_t frames,
                          float *audio, int tanh_out, int threads) {
+    return oracle_vae_chain_stages_f32(topo, P, latent, frames, audio, tanh_out, threads, NULL);
+}
+
+/* Stage s's output (the hidden state after its residual units, src/levo-vae.cpp:230-231)
+ * is copied to stages[s] when stages is non-NULL. */
+int oracle_vae_chain_stages_f32(const int32_t *topo, const float *P, const float *latent, int64_t frames,
+                                float *audio, int tanh_out, int threads, float *const *stages) {
     if (!topo || !P || !latent || !audio || frames <= 0) return -1;
     const int latent_dim = topo[0], audio_channels = topo[1], entry = topo[2], S = topo[3];
     if (S < 1 || S > 8) return -1;
@@ -257,7 +264,13 @@ int oracle_vae_chain_f32(const int32_t *topo, const float *P, const float *laten
     float *a = (float *)malloc(sizeof(float) * (size_t)maxe);
     float *b = (float *)malloc(sizeof(float) * (size_t)maxe);
     float *tmp = (float *)malloc(sizeof(float) * (size_t)maxe);
-    if (!x || !a || !b || !tmp) return -2;
+    if (!x || !a || !b || !tmp) {
+        free(x);
+        free(a);
+        free(b);
+        free(tmp);
+        return -2;
+    }
 
     int64_t off = 0;
     const float *in_bias = P + off;
@@ -296,6 +309,7 @@ int oracle_vae_chain_f32(const int32_t *topo, const float *P, const float *laten
             node(NODE_ADD_ROW, a, NULL, b1, b, cout, lout, threads);         /* conv.1 (id)+b1  */
             node(NODE_ADD, x, b, NULL, x, cout, lout, threads);              /* residual add    */
         }
+        if (stages && stages[s]) memcpy(stages[s], x, sizeof(float) * (size_t)(cout * lout));
         cin = cout;
         len = lout;
     }

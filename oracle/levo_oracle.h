@@ -51,6 +51,10 @@ void oracle_conv_standin_f32(const float *in, int64_t cin, int64_t lin, float *o
  * audio: [audio_channels][frames * prod(strides)]. */
 int oracle_vae_chain_f32(const int32_t *topology, const float *params, const float *latent,
                          int64_t frames, float *audio, int tanh_out, int threads);
+/* The same, also copying stage s's output [widths[s]][frames * prod(strides[0..s])]
+ * to stages[s] (stages NULL or stages[s] NULL: not copied). */
+int oracle_vae_chain_stages_f32(const int32_t *topology, const float *params, const float *latent,
+                                int64_t frames, float *audio, int tanh_out, int threads, float *const *stages);
 
 /* Residual add + RMSNorm / LayerNorm on F16 (IEEE half bits) or F32 rows.
  * RMSNorm: src/levo-lm.cpp:131-138, src/levo-kv.cpp:153-170.

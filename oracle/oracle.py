@@ -30,6 +30,7 @@ _SIGS = {
     "oracle_fused_unit_f32": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _INT, _INT],
     "oracle_conv_standin_f32": [_P, _I64, _I64, _P, _I64, _I64, _INT],
     "oracle_vae_chain_f32": [_P, _P, _P, _I64, _P, _INT, _INT],
+    "oracle_vae_chain_stages_f32": [_P, _P, _P, _I64, _P, _INT, _INT, _P],
     "oracle_add_rmsnorm_f16": [_P, _P, _P, _P, _P, _I64, _I64, _F, _INT, _INT],
     "oracle_add_rmsnorm_f32": [_P, _P, _P, _P, _P, _I64, _I64, _F, _INT],
     "oracle_add_layernorm_f16": [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _INT, _INT],
@@ -145,13 +146,27 @@ def conv_standin(x, cout: int, lout: int, stride: int) -> np.ndarray:
 
 
 def vae_chain(topology_list, params, latent, frames: int, audio_channels: int, samples: int, tanh=False,
-              threads: int = 0) -> np.ndarray:
+              threads: int = 0, stages: bool = False):
+    """Audio [audio_channels][samples]; with stages=True also the list of stage outputs."""
     topo = np.ascontiguousarray(topology_list, dtype=np.int32)
     params, latent = _f32(params), _f32(latent)
     audio = np.empty((audio_channels, samples), dtype=np.float32)
-    rc = lib().oracle_vae_chain_f32(_p(topo), _p(params), _p(latent), frames, _p(audio), 1 if tanh else 0, threads)
+    if not stages:
+        rc = lib().oracle_vae_chain_f32(_p(topo), _p(params), _p(latent), frames, _p(audio), 1 if tanh else 0,
+                                        threads)
+        assert rc == 0
+        return audio
+    n_stages = int(topo[3])
+    widths, strides = topo[4:4 + n_stages], topo[4 + n_stages:4 + 2 * n_stages]
+    outs, length = [], frames
+    for w, s in zip(widths, strides):
+        length *= int(s)
+        outs.append(np.empty((int(w), length), dtype=np.float32))
+    ptrs = (ctypes.c_void_p * n_stages)(*[o.ctypes.data for o in outs])
+    rc = lib().oracle_vae_chain_stages_f32(_p(topo), _p(params), _p(latent), frames, _p(audio), 1 if tanh else 0,
+                                           threads, ctypes.cast(ptrs, ctypes.c_void_p))
     assert rc == 0
-    return audio
+    return audio, outs
 
 
 def _norm(layer: bool, x, r, gamma, beta, eps, f16_boundary, threads):

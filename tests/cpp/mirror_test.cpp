@@ -131,14 +131,39 @@ int main() {
     vae_decoder dec(topo, params, 16);
     std::vector<float> latent(4 * 10);
     for (size_t i = 0; i < latent.size(); ++i) latent[i] = std::sin(0.3F * static_cast<float>(i));
-    const std::vector<float> a1 = dec.decode(latent, 10, true), a2 = dec.decode(latent, 10, true);
-    CHECK(a1.size() == static_cast<size_t>(2 * 10 * 6) && a1 == a2);
+    const vae_decode_result r1 = dec.decode(latent, 10, false, {}, true), r2 = dec.decode(latent, 10, true, {}, true);
+    const std::vector<float> &a1 = r1.audio;
+    CHECK(r1.frames == 10 && r1.samples_per_channel == 60);
+    CHECK(a1.size() == static_cast<size_t>(2 * 10 * 6) && a1 == r2.audio);
     for (float s : a1) CHECK(std::isfinite(s) && std::fabs(s) <= 1.0F);
+    // capture_stages: stage outputs [8][30] and [4][60]; none for the plain decode
+    CHECK(r1.stage_outputs.empty() && r2.stage_outputs.size() == 2);
+    CHECK(r2.stage_outputs.size() == 2 && r2.stage_outputs[0].size() == 8 * 30 && r2.stage_outputs[1].size() == 4 * 60);
+    for (const auto &stage : r2.stage_outputs)
+        for (float v : stage) CHECK(std::isfinite(v));
     thrown = false;
     try {
         (void)dec.decode(latent, 9);
     } catch (const std::runtime_error &e) {
         thrown = std::string(e.what()).rfind("LeVo VAE: ", 0) == 0;
+    }
+    CHECK(thrown);
+    // a non-finite latent is rejected like vae_decoder::decode (src/levo-vae.cpp:189-191)
+    std::vector<float> bad = latent;
+    bad[7] = std::nanf("");
+    thrown = false;
+    try {
+        (void)dec.decode(bad, 10);
+    } catch (const std::runtime_error &e) {
+        thrown = std::string(e.what()).find("non-finite") != std::string::npos;
+    }
+    CHECK(thrown);
+    // cancellation before the work
+    thrown = false;
+    try {
+        (void)dec.decode(latent, 10, false, [] { return true; });
+    } catch (const operation_cancelled &) {
+        thrown = true;
     }
     CHECK(thrown);
 

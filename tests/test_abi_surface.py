@@ -108,6 +108,7 @@ def test_zero_sizes_are_noops_without_gpu(ops):
     assert lib.levo_add_layernorm_f32(p, None, p, p, None, p, 0, 16, 1e-5, 0, None) == ops.OK
     assert lib.levo_weightnorm_f32(p, p, p, None, 0, 7, None) == ops.OK
     assert lib.levo_snake_params_prepare(p, p, 0, 0, p, p, None) == ops.OK
+    assert lib.levo_vae_chain_set_stage_capture(None, None, 0) == ops.EINVAL  # no chain
 
 
 def test_chain_rejects_bad_topology_without_gpu(ops):

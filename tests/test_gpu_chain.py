@@ -34,6 +34,10 @@ def params_for(ops, topo, seed):
     return (0.1 * rng.standard_normal(ops.param_count(topo))).astype(np.float32)
 
 
+def chain_samples(topo, frames):
+    return frames * topo.upsampling()
+
+
 def oracle_audio(orc, topo, params, latent, frames, tanh=False):
     return orc.vae_chain(topo.as_list(), params, latent, frames, topo.audio_channels, frames * topo.upsampling(),
                          tanh=tanh)
@@ -238,3 +242,47 @@ def test_f16_stored_parameters(ops, orc, dev):
     chain32.decode(torch.from_numpy(latent).to(dev), a32, frames, flags=ops.CHAIN_TANH)
     assert torch.equal(a16, a32)
     assert_close(a16.cpu().numpy(), oracle_audio(orc, topo, params16.astype(np.float32), latent, frames, True), TOL)
+
+
+@pytest.mark.parametrize("residual", [0, 2])
+def test_stage_capture_matches_oracle(ops, orc, dev, residual):
+    """capture_stages (src/levo-vae.cpp:230-231,271-274): every stage's output, into device
+    tensors (device decode) and host arrays (host decode); audio unchanged by capturing."""
+    topo = small_topology(ops, residual=residual)
+    params = params_for(ops, topo, 50 + residual)
+    frames = 11
+    latent = np.random.default_rng(51).standard_normal((topo.latent_dim, frames)).astype(np.float32)
+    want_audio, want_stages = orc.vae_chain(topo.as_list(), params, latent, frames, 2, chain_samples(topo, frames),
+                                            stages=True)
+    chain = ops.VaeChain(topo, params, max_frames=frames, device=0)
+    dev_stages = [torch.full(w.shape, np.nan, device=dev) for w in want_stages]
+    chain.set_stage_capture(dev_stages)
+    audio = torch.empty((2, chain.samples(frames)), device=dev)
+    chain.decode(torch.from_numpy(latent).to(dev), audio, frames)
+    torch.cuda.synchronize()
+    assert_close(audio.cpu().numpy(), want_audio, TOL)
+    for got, want in zip(dev_stages, want_stages):
+        assert_close(got.cpu().numpy(), want, TOL)
+    host_stages = [np.full(w.shape, np.nan, np.float32) for w in want_stages]
+    chain.set_stage_capture(host_stages)
+    host_audio = np.empty((1, 2, chain.samples(frames)), np.float32)
+    chain.decode_windows(latent[None], host_audio, frames)
+    for got, want in zip(host_stages, want_stages):
+        assert_close(got, want, TOL)
+    assert np.array_equal(host_audio[0], audio.cpu().numpy())
+    with pytest.raises(ValueError, match="one window"):
+        chain.decode_windows(np.stack([latent, latent]), np.empty((2, 2, chain.samples(frames)), np.float32), frames)
+    chain.set_stage_capture(None)
+    chain.decode_windows(np.stack([latent, latent]), np.empty((2, 2, chain.samples(frames)), np.float32), frames)
+
+
+def test_decode_windows_rejects_non_finite_latent(ops, dev):
+    # vae_decoder::decode: "latent payload contains a non-finite value" (src/levo-vae.cpp:189-191)
+    topo = small_topology(ops)
+    chain = ops.VaeChain(topo, params_for(ops, topo, 52), max_frames=6, device=0)
+    lat = np.random.default_rng(52).standard_normal((3, topo.latent_dim, 6)).astype(np.float32)
+    lat[1, 3, 2] = np.inf
+    out = np.full((3, 2, chain.samples(6)), np.nan, np.float32)
+    with pytest.raises(ops.LevoOpsError, match="non-finite value \\(window 1\\)"):
+        chain.decode_windows(lat, out, 6)
+    assert np.all(np.isfinite(out[0])) and np.all(np.isnan(out[1:]))
