@@ -24,6 +24,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "common.cuh"
 
 namespace levo {
@@ -183,6 +185,21 @@ class DeviceGuard {
     int previous_ = -1;
 };
 
+// NVTX range for profilers (ncu --nvtx, Nsight Systems): one per decoded window
+// and per decoder stage.  Header-only NVTX v3: without an attached tool each
+// push / pop is a few nanoseconds.
+class NvtxRange {
+   public:
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+
+constexpr const char *kStageRangeNames[LEVO_VAE_MAX_STAGES] = {
+    "levo.vae.stage0", "levo.vae.stage1", "levo.vae.stage2", "levo.vae.stage3",
+    "levo.vae.stage4", "levo.vae.stage5", "levo.vae.stage6", "levo.vae.stage7"};
+
 struct TimedLaunch {
     int kclass;
     int ev_start, ev_end;
@@ -327,6 +344,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
     const size_t esize = c->pdtype == LEVO_DTYPE_F16 ? 2 : 4;
     const char *base = static_cast<const char *>(c->params);
     auto P = [&](int64_t off) -> const void * { return base + off * esize; };
+    NvtxRange window_range("levo.vae.decode");
     const bool timing = (flags & LEVO_CHAIN_TIMING) != 0;
     const bool capturing = c->n_capture > 0;
     auto snake_of = [&](int stage, int unit) -> SnakeRef {
@@ -373,6 +391,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
     int64_t cin = t.entry_width;
     int64_t len = frames;
     for (int st = 0; st < t.n_stages; ++st) {
+        NvtxRange stage_range(kStageRangeNames[st]);
         const int64_t cout = t.stage_width[st];
         const int64_t lout = len * t.stage_stride[st];
         const StageOffsets &so = l.stage[st];
