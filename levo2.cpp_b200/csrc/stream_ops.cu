@@ -3,8 +3,9 @@
 //
 // Each is a single HBM pass: every input element is read once with a 256-bit
 // load and every output written once with a 256-bit store.  Two vector forms:
-//  * rows form (rows of a multiple of 8 values, 32-byte aligned tensors, the
-//    decoder's case): the tensor is cut into row chunks of kRowThreads*UNROLL
+//  * rows form (dense rows, 32-byte aligned tensors: the decoder's case; rows
+//    that are not a multiple of 8 long get a scalar head and tail around a
+//    vector body): the tensor is cut into row chunks of kRowThreads*UNROLL
 //    vectors and a grid far larger than the resident CTA count walks them, so
 //    the channel is uniform per chunk and its parameters (alpha, 1/beta, bias:
 //    promoted to F32 and exponentiated) are computed in registers per chunk.
@@ -33,6 +34,9 @@ constexpr int kUnroll = 2;
 //    one CTA per chunk, 5.90 with 1x).
 constexpr int kRowThreads = 128;
 constexpr int kResidualGridPerResident = 16;
+// Shortest row length that is not a multiple of 8 the rows form takes: the head
+// (< 8) stays inside the row and the body holds at least one vector.
+constexpr int64_t kMinRaggedRow = 64;
 constexpr int64_t kMaxStagedChannels = 4096;
 
 struct StreamArgs {
@@ -120,7 +124,7 @@ __device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelPar
 // persistent grid (a plain 2-in/2-out stream on B200: ~6.8 against ~6.0 TB/s),
 // so G is far above the resident CTA count (launch_rows).  The loads of a
 // chunk are issued before its channel parameters are computed.
-template <bool HAS_RES, bool SNAKE, int UNROLL>
+template <bool HAS_RES, bool SNAKE, int UNROLL, bool RAGGED>
 __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamArgs a) {
     pdl_wait();
     pdl_trigger();
@@ -130,26 +134,43 @@ __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamAr
     int64_t c = row_of(q0, a.chunks_per_row, a.inv_chunks_per_row);
     int64_t k = q0 - c * a.chunks_per_row;
     for (int64_t q = q0; q < q1; ++q) {
-        const size_t row = static_cast<size_t>(c) * a.len;
+        // A row whose length is not a multiple of 8 starts at any 4-byte phase:
+        // scalar head up to its first 32-byte boundary, 256-bit body, scalar tail.
+        const int64_t row = c * a.len;
+        const int64_t head = RAGGED ? ((-row) & 7) : 0;
+        const int64_t body = RAGGED ? (a.len - head) >> 3 : a.vec_per_row;
+        const size_t base = static_cast<size_t>(row + head);
         const int64_t v0 = k * (kRowThreads * UNROLL) + threadIdx.x;
         f32x8 uu[UNROLL], rr[UNROLL];
 #pragma unroll
         for (int j = 0; j < UNROLL; ++j) {
             const int64_t v = v0 + j * kRowThreads;
-            if (v < a.vec_per_row) {
-                uu[j] = ld8(a.u + row + v * 8);
-                if (HAS_RES) rr[j] = ld8(a.res + row + v * 8);
+            if (v < body) {
+                uu[j] = ld8(a.u + base + v * 8);
+                if (HAS_RES) rr[j] = ld8(a.res + base + v * 8);
             }
         }
         const ChannelParams p = channel_params<SNAKE>(a, nullptr, c);
 #pragma unroll
         for (int j = 0; j < UNROLL; ++j) {
             const int64_t v = v0 + j * kRowThreads;
-            if (v >= a.vec_per_row) continue;
+            if (v >= body) continue;
             f32x8 xo, yo;
             unit_eval8<HAS_RES, SNAKE>(a, p, uu[j], rr[j], xo, yo);
-            if (a.write_x) st8(a.x_out + row + v * 8, xo);
-            if (a.write_y) st8(a.y_out + row + v * 8, yo);
+            if (a.write_x) st8(a.x_out + base + v * 8, xo);
+            if (a.write_y) st8(a.y_out + base + v * 8, yo);
+        }
+        if (RAGGED && k == 0) {
+            // head + tail < 16 <= kRowThreads elements, one per thread
+            const int64_t tail = a.len - head - body * 8;
+            const int64_t t = threadIdx.x;
+            if (t < head + tail) {
+                const int64_t e = t < head ? row + t : row + head + body * 8 + (t - head);
+                float xs, ys;
+                unit_eval<HAS_RES, SNAKE>(a, p, a.u[e], HAS_RES ? a.res[e] : 0.f, xs, ys);
+                if (a.write_x) a.x_out[e] = xs;
+                if (a.write_y) a.y_out[e] = ys;
+            }
         }
         if (++k == a.chunks_per_row) {
             k = 0;
@@ -277,9 +298,11 @@ __global__ void __launch_bounds__(kThreads) stream_scalar_kernel(const StreamArg
 template <bool HAS_RES, bool SNAKE>
 int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
     constexpr int kRowUnroll = HAS_RES ? 1 : 4;
-    auto kernel = stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll>;
+    const bool ragged = a.len % 8 != 0;
+    auto kernel = ragged ? stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, true>
+                         : stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, false>;
     a.staged = 0;
-    a.vec_per_row = a.len / 8;
+    a.vec_per_row = a.len / 8;  // a ragged row's body has vec_per_row or vec_per_row - 1 vectors
     a.chunks_per_row = (a.vec_per_row + kRowThreads * kRowUnroll - 1) / (kRowThreads * kRowUnroll);
     a.chunks = a.rows * a.chunks_per_row;
     a.inv_chunks_per_row = 1.0 / static_cast<double>(a.chunks_per_row);
@@ -288,13 +311,14 @@ int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
     int64_t cap = 0x7fffffff;
     if (HAS_RES) {
         // resident CTAs per SM: a property of the kernel and the architecture, queried once
-        static const int per_sm = [kernel] {
+        auto resident = [](auto k) {
             int n = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kRowThreads, 0) != cudaSuccess || n <= 0)
-                n = 1;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kRowThreads, 0) != cudaSuccess || n <= 0) n = 1;
             return n;
-        }();
-        cap = static_cast<int64_t>(sm_count()) * per_sm * kResidualGridPerResident;
+        };
+        static const int per_sm_aligned = resident(stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, false>);
+        static const int per_sm_ragged = resident(stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, true>);
+        cap = static_cast<int64_t>(sm_count()) * (ragged ? per_sm_ragged : per_sm_aligned) * kResidualGridPerResident;
     }
     const int64_t grid = std::min<int64_t>(a.chunks, cap);
     const cudaError_t err = launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kRowThreads), 0, stream, a);
@@ -415,8 +439,9 @@ int run_stream(const StreamRequest &q, cudaStream_t stream, const char *what) {
         if (a.nvec == 0) vec = false;
     }
 
-    // Rows form: dense rows of a multiple of 8 values, every tensor 32-byte aligned.
-    if (vec && a.head == 0 && q.len % 8 == 0) {
+    // Rows form: dense rows, every tensor 32-byte aligned; rows of a multiple of 8
+    // values, or at least kMinRaggedRow (then each row has a scalar head and tail).
+    if (vec && a.head == 0 && (q.len % 8 == 0 || q.len >= kMinRaggedRow)) {
         if (q.res)
             return snake ? launch_rows<true, true>(a, stream, what) : launch_rows<true, false>(a, stream, what);
         return snake ? launch_rows<false, true>(a, stream, what) : launch_rows<false, false>(a, stream, what);
