@@ -124,6 +124,14 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Waits until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Parameters
 // ---------------------------------------------------------------------------
@@ -168,22 +176,61 @@ __device__ __forceinline__ float snake_inv_beta_param(const void *p, int64_t c, 
 // to sin_squared_any(), which uses CUDA's sinf and its large-argument reduction.
 constexpr float kSin2FastLimit = 65536.0f;
 
+// The constants of the three steps above (shared by the scalar and paired forms).
+constexpr float kSin2Big = 12582912.0f;                 // 1.5 * 2^23
+constexpr float kSin2TwoOverPi = 0.636619747f;
+constexpr float kSin2PiOver2A = 1.57079637f;  // pi/2 = A + B + C
+constexpr float kSin2PiOver2B = -4.37113883e-08f;
+constexpr float kSin2PiOver2C = -1.77635684e-15f;
+constexpr float kSin2Q0 = -4.103582341e-06f;  // Q(z) = ((((Q0 z + Q1) z + Q2) z + Q3) z + Q4) z + Q5
+constexpr float kSin2Q1 = 1.409736724e-04f;
+constexpr float kSin2Q2 = -3.174564568e-03f;
+constexpr float kSin2Q3 = 4.444443807e-02f;
+constexpr float kSin2Q4 = -3.333333433e-01f;
+constexpr float kSin2Q5 = 1.0f;
+
+// Every step rounds on its own (explicit _rn operations, no contraction), so the
+// paired form below gives the same bits.
 __device__ __forceinline__ float sin_squared_fast(float t) {
-    const float kBig = 12582912.0f;  // 1.5 * 2^23
-    const float ks = fmaf(t, 0.636619747f, kBig);
+    const float ks = __fmaf_rn(t, kSin2TwoOverPi, kSin2Big);
     const int odd = __float_as_int(ks) & 1;
-    const float k = ks - kBig;
-    float r = fmaf(-k, 1.57079637f, t);
-    r = fmaf(-k, -4.37113883e-08f, r);
-    r = fmaf(-k, -1.77635684e-15f, r);
-    const float z = r * r;
-    float q = fmaf(z, -4.103582341e-06f, 1.409736724e-04f);
-    q = fmaf(q, z, -3.174564568e-03f);
-    q = fmaf(q, z, 4.444443807e-02f);
-    q = fmaf(q, z, -3.333333433e-01f);
-    q = fmaf(q, z, 1.0f);
-    const float p = z * q;
-    return odd ? 1.0f - p : p;
+    const float k = __fadd_rn(ks, -kSin2Big);
+    float r = __fmaf_rn(k, -kSin2PiOver2A, t);
+    r = __fmaf_rn(k, -kSin2PiOver2B, r);
+    r = __fmaf_rn(k, -kSin2PiOver2C, r);
+    const float z = __fmul_rn(r, r);
+    float q = __fmaf_rn(z, kSin2Q0, kSin2Q1);
+    q = __fmaf_rn(q, z, kSin2Q2);
+    q = __fmaf_rn(q, z, kSin2Q3);
+    q = __fmaf_rn(q, z, kSin2Q4);
+    q = __fmaf_rn(q, z, kSin2Q5);
+    const float p = __fmul_rn(z, q);
+    return odd ? __fadd_rn(1.0f, -p) : p;
+}
+
+// Two arguments at once with sm_100's paired F32 instructions (__ffma2_rn,
+// __fmul2_rn, __fadd2_rn: each lane one IEEE round-to-nearest operation), so the
+// result is bit-identical to two sin_squared_fast calls in half the arithmetic
+// instructions.
+__device__ __forceinline__ float2 pair(float v) { return make_float2(v, v); }
+
+__device__ __forceinline__ float2 sin_squared_fast2(float2 t) {
+    const float2 ks = __ffma2_rn(t, pair(kSin2TwoOverPi), pair(kSin2Big));
+    const int odd_x = __float_as_int(ks.x) & 1;
+    const int odd_y = __float_as_int(ks.y) & 1;
+    const float2 k = __fadd2_rn(ks, pair(-kSin2Big));
+    float2 r = __ffma2_rn(k, pair(-kSin2PiOver2A), t);
+    r = __ffma2_rn(k, pair(-kSin2PiOver2B), r);
+    r = __ffma2_rn(k, pair(-kSin2PiOver2C), r);
+    const float2 z = __fmul2_rn(r, r);
+    float2 q = __ffma2_rn(z, pair(kSin2Q0), pair(kSin2Q1));
+    q = __ffma2_rn(q, z, pair(kSin2Q2));
+    q = __ffma2_rn(q, z, pair(kSin2Q3));
+    q = __ffma2_rn(q, z, pair(kSin2Q4));
+    q = __ffma2_rn(q, z, pair(kSin2Q5));
+    const float2 p = __fmul2_rn(z, q);
+    const float2 om = __fadd2_rn(pair(1.0f), make_float2(-p.x, -p.y));
+    return make_float2(odd_x ? om.x : p.x, odd_y ? om.y : p.y);
 }
 
 __device__ __forceinline__ float sin_squared_any(float t) {
@@ -201,19 +248,26 @@ __device__ __forceinline__ float snake_eval(float x, float alpha, float inv_beta
 // SnakeBeta of 8 values of one channel: one range check per vector, then the
 // branch-free fast path (the common case) or the general one.
 __device__ __forceinline__ void snake_eval8(float (&v)[8], float alpha, float inv_beta) {
-    float t[8];
+    float2 t[4];
     float m = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        t[k] = __fmul_rn(v[k], alpha);
-        m = fmaxf(m, fabsf(t[k]));
+    for (int k = 0; k < 4; ++k) {
+        t[k] = __fmul2_rn(make_float2(v[2 * k], v[2 * k + 1]), pair(alpha));
+        m = fmaxf(m, fmaxf(fabsf(t[k].x), fabsf(t[k].y)));
     }
     if (m <= kSin2FastLimit) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = __fmaf_rn(sin_squared_fast(t[k]), inv_beta, v[k]);
+        for (int k = 0; k < 4; ++k) {
+            const float2 y = __ffma2_rn(sin_squared_fast2(t[k]), pair(inv_beta), make_float2(v[2 * k], v[2 * k + 1]));
+            v[2 * k] = y.x;
+            v[2 * k + 1] = y.y;
+        }
     } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = __fmaf_rn(sin_squared_any(t[k]), inv_beta, v[k]);
+        for (int k = 0; k < 4; ++k) {
+            v[2 * k] = __fmaf_rn(sin_squared_any(t[k].x), inv_beta, v[2 * k]);
+            v[2 * k + 1] = __fmaf_rn(sin_squared_any(t[k].y), inv_beta, v[2 * k + 1]);
+        }
     }
 }
 

@@ -217,3 +217,18 @@ def test_fused_unit_prepared_params(ops, dev):
     ops.fused_unit_t(u, bias, r, a, b, out[0], out[1])
     ops.fused_unit_t(u, bias, r, alpha, inv_beta, out[2], out[3], param_dtype=ops.DTYPE_SNAKE_PREPARED)
     assert torch.equal(out[0], out[2]) and torch.equal(out[1], out[3])
+
+
+@pytest.mark.parametrize("scale", [1.0, 3e4])
+def test_snakebeta_vector_and_scalar_paths_agree_bitwise(ops, dev, scale):
+    """The paired-F32 vector path and the scalar path round every step alike: same bits,
+    on the fast range and past the sinf fallback limit (|x*alpha| > 65536)."""
+    rng = np.random.default_rng(61)
+    c, t = 24, 4096
+    x = torch.from_numpy((scale * rng.standard_normal((c, t))).astype(np.float32)).to(dev)
+    a, b = (torch.from_numpy(p).to(dev) for p in _params(rng, c, scale=1.0))
+    dense = ops.snakebeta_t(x, a, b)
+    wide = torch.empty((c, t + 3), device=dev)
+    wide[:, :t] = x
+    strided = ops.snakebeta_t(wide[:, :t], a, b)  # row stride t + 3: scalar path
+    assert torch.equal(dense, strided)
