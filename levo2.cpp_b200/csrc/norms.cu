@@ -382,12 +382,17 @@ __device__ __forceinline__ void norm_row_from_smem(const NormArgs &a, int64_t ro
         float h[N];
         const bool gated = MOD && a.gate;
         if (!gated && has_r) {
-            // plain residual add, in the activation type
+            // plain residual add, in the activation type; sums on paired F32 lanes
             const uint4 hc = Chunk<T>::add(xs[i], rs[i]);
             xs[i] = hc;
             Chunk<T>::unpack(hc, h);
+            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int j = 0; j < N; ++j) sum += LAYER ? h[j] : h[j] * h[j];
+            for (int j = 0; j < N; j += 2) {
+                const float2 v = make_float2(h[j], h[j + 1]);
+                acc = LAYER ? __fadd2_rn(acc, v) : __ffma2_rn(v, v, acc);
+            }
+            sum += acc.x + acc.y;
             continue;
         }
         Chunk<T>::unpack(xs[i], h);
@@ -419,11 +424,13 @@ __device__ __forceinline__ void norm_row_from_smem(const NormArgs &a, int64_t ro
         for (int i = lane; i < chunks; i += 32) {
             float h[N];
             Chunk<T>::unpack(xs[i], h);
+            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int j = 0; j < N; ++j) {
-                const float d = __fsub_rn(h[j], mean);
-                sq += d * d;
+            for (int j = 0; j < N; j += 2) {
+                const float2 d = __fadd2_rn(make_float2(h[j], h[j + 1]), pair(-mean));
+                acc = __ffma2_rn(d, d, acc);
             }
+            sq += acc.x + acc.y;
         }
         sq = warp_sum(sq);
         scale = 1.0f / sqrtf(sq * inv_dim + a.eps);
@@ -444,12 +451,20 @@ __device__ __forceinline__ void norm_row_from_smem(const NormArgs &a, int64_t ro
         float ms[N], mh[N];
         if (MOD && a.scale) load_cols<N>(a.scale + mod_off + i * N, ms);
         if (MOD && a.shift) load_cols<N>(a.shift + mod_off + i * N, mh);
+        // n = (h [- mean]) * scale, y = n * gamma [+ beta] [* (1 + s) + shift]: the same
+        // rounded steps as norm_output / modulate, two columns per instruction
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-            const float n = LAYER ? __fmul_rn(__fsub_rn(h[j], mean), scale) : __fmul_rn(h[j], scale);
-            float y = norm_output<T, LAYER>(a, n, g[j], LAYER ? b[j] : 0.f);
-            if (MOD) y = modulate(a, y, (a.scale ? ms[j] : 0.f), (a.shift ? mh[j] : 0.f));
-            h[j] = y;
+        for (int j = 0; j < N; j += 2) {
+            float2 v = make_float2(h[j], h[j + 1]);
+            if (LAYER) v = __fadd2_rn(v, pair(-mean));
+            v = __fmul2_rn(v, pair(scale));
+            if (a.f16_boundary) v = make_float2(Act<T>::round(v.x), Act<T>::round(v.y));
+            v = __fmul2_rn(v, make_float2(g[j], g[j + 1]));
+            if (LAYER) v = __fadd2_rn(v, make_float2(b[j], b[j + 1]));
+            if (MOD && a.scale) v = __fmul2_rn(v, __fadd2_rn(make_float2(ms[j], ms[j + 1]), pair(1.0f)));
+            if (MOD && a.shift) v = __fadd2_rn(v, make_float2(mh[j], mh[j + 1]));
+            h[j] = v.x;
+            h[j + 1] = v.y;
         }
         yg[i] = Chunk<T>::pack(h);
     }
@@ -483,55 +498,6 @@ __global__ void __launch_bounds__(kStagedRows * 32) add_norm_staged_kernel(const
         __syncwarp();
         norm_row_from_smem<T, LAYER, MOD>(a, row, xs, rs, lane, chunks, inv_dim);
     }
-}
-
-// Pipelined form: each warp walks rows warp, warp + W, ... (W = all warps of
-// the grid, so a round covers contiguous rows) with kPipeStages rows in flight
-// per warp in cp.async groups; row i is processed while rows i+1.. land, so
-// the writes of finished rows overlap the reads of later ones.
-constexpr int kPipeWarps = 8;
-constexpr int kPipeStages = 2;
-constexpr int kPipeCtasPerSm = 1;
-constexpr bool kUsePipelined = false;
-
-template <typename T, bool LAYER, bool MOD>
-__global__ void __launch_bounds__(kPipeWarps * 32) add_norm_pipelined_kernel(const NormArgs a) {
-    extern __shared__ uint4 sbuf[];
-    constexpr int N = Chunk<T>::kN;
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int chunks = a.dim / N;
-    const float inv_dim = 1.0f / static_cast<float>(a.dim);
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * kPipeWarps;
-    const int64_t first = static_cast<int64_t>(blockIdx.x) * kPipeWarps + warp;
-    uint4 *wbuf = sbuf + static_cast<size_t>(warp) * kPipeStages * 2 * chunks;
-    auto issue = [&](int64_t row, int stage) {
-        if (row < a.rows) {
-            uint4 *xs = wbuf + static_cast<size_t>(stage) * 2 * chunks;
-            const uint4 *xg =
-                reinterpret_cast<const uint4 *>(static_cast<const char *>(a.x) + row * a.dim * sizeof(T));
-            for (int i = lane; i < chunks; i += 32) cp_async16(xs + i, xg + i);
-            if (a.r) {
-                const uint4 *rg =
-                    reinterpret_cast<const uint4 *>(static_cast<const char *>(a.r) + row * a.dim * sizeof(T));
-                for (int i = lane; i < chunks; i += 32) cp_async16(xs + chunks + i, rg + i);
-            }
-        }
-        cp_async_commit();  // one group per row slot, empty past the last row
-    };
-#pragma unroll
-    for (int st = 0; st < kPipeStages; ++st) issue(first + st * stride, st);
-    int stage = 0;
-    for (int64_t row = first; row < a.rows; row += stride) {
-        cp_async_wait_group<kPipeStages - 1>();  // this row's group has landed
-        __syncwarp();
-        uint4 *xs = wbuf + static_cast<size_t>(stage) * 2 * chunks;
-        norm_row_from_smem<T, LAYER, MOD>(a, row, xs, xs + chunks, lane, chunks, inv_dim);
-        __syncwarp();  // every lane is done with this slot before it is refilled
-        issue(row + kPipeStages * stride, stage);
-        stage = stage + 1 == kPipeStages ? 0 : stage + 1;
-    }
-    cp_async_wait_all();
 }
 
 // Fallback: one CTA per row, any dim and alignment.
@@ -638,26 +604,6 @@ int run_norm(const char *what, const void *x, const void *r, const float *gamma,
             if (ptrs[i] && !aligned_to(ptrs[i], 16)) staged = false;
         for (const void *m : mods)
             if (m && !aligned_to(m, 16)) staged = false;
-        if (staged && kUsePipelined) {
-            const size_t psmem = static_cast<size_t>(kPipeWarps) * kPipeStages * 2 * dim * sizeof(T);
-            auto kernel = add_norm_pipelined_kernel<T, LAYER, MOD>;
-            bool ok = psmem <= kStagedMaxSmem;
-            if (ok && psmem > 48 * 1024)
-                ok = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(psmem)) == cudaSuccess;
-            if (ok) {
-                int per_sm = 0;
-                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kPipeWarps * 32, psmem) !=
-                        cudaSuccess ||
-                    per_sm <= 0)
-                    per_sm = 1;
-                per_sm = std::min(per_sm, kPipeCtasPerSm);
-                const int64_t grid = std::min<int64_t>((rows + kPipeWarps - 1) / kPipeWarps,
-                                                       static_cast<int64_t>(sm_count()) * per_sm);
-                kernel<<<static_cast<unsigned>(grid), kPipeWarps * 32, psmem, stream>>>(a);
-                return check_launch(what);
-            }
-        }
         if (staged) {
             auto kernel = add_norm_staged_kernel<T, LAYER, MOD>;
             if (smem > 48 * 1024 &&
