@@ -6,9 +6,9 @@
 //  * rows form (dense rows, 32-byte aligned tensors: the decoder's case; rows
 //    that are not a multiple of 8 long get a scalar head and tail around a
 //    vector body): the tensor is cut into row chunks of kRowThreads*UNROLL
-//    vectors and a grid far larger than the resident CTA count walks them, so
-//    the channel is uniform per chunk and its parameters (alpha, 1/beta, bias:
-//    promoted to F32 and exponentiated) are computed in registers per chunk.
+//    vectors, one CTA per chunk, so the channel is uniform per CTA and its
+//    parameters (alpha, 1/beta, bias: promoted to F32 and exponentiated) are
+//    computed once in registers.
 //  * flat form (any row length, any common 32-byte phase): one CTA per tile of
 //    the flat element space; parameters are cached per thread by channel (or
 //    staged in shared memory when there are few channels), and a vector that
@@ -24,16 +24,14 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 2;
-// Rows form: 128-thread CTAs.  Measured on the config-4 chain (sweep of block
-// size 128-256, unroll 1-8 and grid size) on B200:
+// Rows form: 128-thread CTAs, one CTA per chunk.  Measured on the config-4
+// chain (sweep of block size 128-256, unroll 1-8 and grid size) on B200:
 //  * 1-input units (SnakeBeta, post / upsample units): four vectors per thread
-//    per chunk and one CTA per chunk (~6.0-6.5 TB/s; a grid of resident CTAs
-//    walking chunk ranges reached ~5.2-5.5);
-//  * 2-input residual unit: one vector per thread per chunk and a grid of 16x
-//    the resident CTAs, each walking a short chunk range (6.18 TB/s; 5.88 with
-//    one CTA per chunk, 5.90 with 1x).
+//    per chunk (6.1-6.4 TB/s; a grid of resident CTAs walking chunk ranges
+//    reached 5.2-5.5);
+//  * 2-input residual unit: two vectors per thread per chunk (6.26 TB/s; one
+//    vector with 16x the resident CTAs walking chunk ranges: 6.20).
 constexpr int kRowThreads = 128;
-constexpr int kResidualGridPerResident = 16;
 // Shortest row length that is not a multiple of 8 the rows form takes: the head
 // (< 8) stays inside the row and the body holds at least one vector.
 constexpr int64_t kMinRaggedRow = 64;
@@ -122,7 +120,7 @@ __device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelPar
 // vectors [k*kRowThreads*UNROLL, (k+1)*kRowThreads*UNROLL) of row c, q = c*cpr + k.
 // Short-lived CTAs that the block scheduler refills keep HBM busier than a
 // persistent grid (a plain 2-in/2-out stream on B200: ~6.8 against ~6.0 TB/s),
-// so G is far above the resident CTA count (launch_rows).  The loads of a
+// so launch_rows gives every chunk its own CTA (G = chunks).  The loads of a
 // chunk are issued before its channel parameters are computed.
 template <bool HAS_RES, bool SNAKE, int UNROLL, bool RAGGED>
 __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamArgs a) {
@@ -297,7 +295,7 @@ __global__ void __launch_bounds__(kThreads) stream_scalar_kernel(const StreamArg
 
 template <bool HAS_RES, bool SNAKE>
 int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
-    constexpr int kRowUnroll = HAS_RES ? 1 : 4;
+    constexpr int kRowUnroll = HAS_RES ? 2 : 4;
     const bool ragged = a.len % 8 != 0;
     auto kernel = ragged ? stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, true>
                          : stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, false>;
@@ -306,21 +304,8 @@ int launch_rows(StreamArgs a, cudaStream_t stream, const char *what) {
     a.chunks_per_row = (a.vec_per_row + kRowThreads * kRowUnroll - 1) / (kRowThreads * kRowUnroll);
     a.chunks = a.rows * a.chunks_per_row;
     a.inv_chunks_per_row = 1.0 / static_cast<double>(a.chunks_per_row);
-    // 1-input units: one CTA per chunk (past 2^31 - 1 chunks a CTA takes a
-    // contiguous range); residual unit: 16x the resident CTAs.
-    int64_t cap = 0x7fffffff;
-    if (HAS_RES) {
-        // resident CTAs per SM: a property of the kernel and the architecture, queried once
-        auto resident = [](auto k) {
-            int n = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kRowThreads, 0) != cudaSuccess || n <= 0) n = 1;
-            return n;
-        };
-        static const int per_sm_aligned = resident(stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, false>);
-        static const int per_sm_ragged = resident(stream_rows_kernel<HAS_RES, SNAKE, kRowUnroll, true>);
-        cap = static_cast<int64_t>(sm_count()) * (ragged ? per_sm_ragged : per_sm_aligned) * kResidualGridPerResident;
-    }
-    const int64_t grid = std::min<int64_t>(a.chunks, cap);
+    // one CTA per chunk; past 2^31 - 1 chunks a CTA takes a contiguous range of them
+    const int64_t grid = std::min<int64_t>(a.chunks, 0x7fffffff);
     const cudaError_t err = launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kRowThreads), 0, stream, a);
     if (err != cudaSuccess)
         return set_error(LEVO_OPS_ELAUNCH, std::string(what) + ": kernel launch failed: " + cudaGetErrorString(err));
