@@ -272,6 +272,23 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
                                                uint32_t flags, levo_cancel_fn cancel,
                                                void *cancel_user, levo_stream_t stream);
 
+/*
+ * DECODE over several GPUs from one process, for a host like the reference's
+ * engine (run_decode, src/cantor-abi.cpp:828-925), whose windows are
+ * independent (src/levo-render.cpp:442-451): chains[i] (one per device, one
+ * topology) decodes the contiguous block [i*W/n .. (i+1)*W/n) of the W windows
+ * (block sizes differ by at most one) on its own host thread and its own
+ * stream, writing straight into audio_host.  Each block runs as
+ * levo_vae_chain_decode_windows (non-finite latent check included); `cancel`
+ * is polled by every thread before each of its windows and must be safe to
+ * call from several threads.  Returns after every block is in host memory;
+ * on failure, the lowest failing chain's status and message (with its index).
+ */
+LEVO_OPS_API int levo_vae_chains_decode_windows(levo_vae_chain *const *chains, int32_t n_chains,
+                                                const float *latents_host, int64_t windows, int64_t frames,
+                                                float *audio_host, uint32_t flags, levo_cancel_fn cancel,
+                                                void *cancel_user);
+
 /* Kernel classes timed with LEVO_CHAIN_TIMING. */
 typedef enum {
     LEVO_KCLASS_ENTRY = 0,      /* conv_in bias + first SnakeBeta        8 B/elem */

@@ -22,6 +22,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include <nvtx3/nvToolsExt.h>
@@ -799,6 +800,63 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
     err = cudaStreamSynchronize(chain->copy_stream);
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
     if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: synchronize");
+    return LEVO_OPS_OK;
+}
+
+LEVO_OPS_API int levo_vae_chains_decode_windows(levo_vae_chain *const *chains, int32_t n_chains,
+                                                const float *latents_host, int64_t windows, int64_t frames,
+                                                float *audio_host, uint32_t flags, levo_cancel_fn cancel,
+                                                void *cancel_user) {
+    using namespace levo;
+    clear_error();
+    const char *w = "levo_vae_chains_decode_windows";
+    if (chains == nullptr || n_chains <= 0)
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": at least one chain is required");
+    for (int32_t i = 0; i < n_chains; ++i) {
+        if (chains[i] == nullptr) return set_error(LEVO_OPS_EINVAL, std::string(w) + ": chain is null");
+        if (std::memcmp(&chains[i]->topo, &chains[0]->topo, sizeof(levo_vae_topology)) != 0)
+            return set_error(LEVO_OPS_EINVAL, std::string(w) + ": chains must share one topology");
+        const int rc = check_decode_args(chains[i], frames, flags, w);
+        if (rc != LEVO_OPS_OK) return rc;
+    }
+    if (latents_host == nullptr || audio_host == nullptr || windows < 0)
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": invalid host buffers or window count");
+    const levo_vae_topology &t = chains[0]->topo;
+    const int64_t lat_elems = static_cast<int64_t>(t.latent_dim) * frames;
+    const int64_t audio_elems = static_cast<int64_t>(t.audio_channels) * frames * total_upsampling(t);
+    std::vector<int> codes(static_cast<size_t>(n_chains), LEVO_OPS_OK);
+    std::vector<std::string> messages(static_cast<size_t>(n_chains));
+    auto work = [&](int32_t i) {
+        // contiguous block [start, stop) of the windows, sizes differing by at most one
+        const int64_t base = windows / n_chains, extra = windows % n_chains;
+        const int64_t start = i * base + std::min<int64_t>(i, extra);
+        const int64_t count = base + (i < extra ? 1 : 0);
+        if (count == 0) return;
+        levo_vae_chain *c = chains[i];
+        DeviceGuard guard(c->device);
+        cudaStream_t stream = nullptr;
+        cudaError_t err = cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking);
+        int rc = err == cudaSuccess ? LEVO_OPS_OK : cuda_fail(err, std::string(w) + ": stream");
+        if (rc == LEVO_OPS_OK)
+            rc = levo_vae_chain_decode_windows(c, latents_host + start * lat_elems, count, frames,
+                                               audio_host + start * audio_elems, flags, cancel, cancel_user,
+                                               reinterpret_cast<levo_stream_t>(stream));
+        if (stream != nullptr) cudaStreamDestroy(stream);
+        codes[static_cast<size_t>(i)] = rc;
+        if (rc != LEVO_OPS_OK) messages[static_cast<size_t>(i)] = levo_ops_last_error();
+    };
+    std::vector<std::thread> threads;
+    threads.reserve(static_cast<size_t>(n_chains));
+    for (int32_t i = 1; i < n_chains; ++i) threads.emplace_back(work, i);
+    work(0);
+    for (std::thread &th : threads) th.join();
+    for (int32_t i = 0; i < n_chains; ++i)
+        if (codes[static_cast<size_t>(i)] != LEVO_OPS_OK) {
+            const int64_t start = i * (windows / n_chains) + std::min<int64_t>(i, windows % n_chains);
+            return set_error(codes[static_cast<size_t>(i)],
+                             messages[static_cast<size_t>(i)] + " (chain " + std::to_string(i) +
+                                 ", whose windows start at " + std::to_string(start) + ")");
+        }
     return LEVO_OPS_OK;
 }
 

@@ -132,6 +132,7 @@ SIGNATURES = {
     "levo_vae_chain_set_stage_capture": (_INT, [_P, _P, _I32]),
     "levo_vae_chain_decode": (_INT, [_P, _P, _I64, _P, _U32, _P]),
     "levo_vae_chain_decode_windows": (_INT, [_P, _P, _I64, _I64, _P, _U32, CANCEL_FN, _P, _P]),
+    "levo_vae_chains_decode_windows": (_INT, [_P, _I32, _P, _I64, _I64, _P, _U32, CANCEL_FN, _P]),
     "levo_vae_chain_timing": (_INT, [_P, ctypes.POINTER(KernelTiming), _INT]),
     "levo_conv_standin_f32": (_INT, [_P, _I64, _I64, _P, _I64, _I64, _I32, _P]),
     "levo_add_rmsnorm_f16": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _F, _U32, _P]),
@@ -438,6 +439,17 @@ def param_count(topology: Topology) -> int:
     if n < 0:
         check(int(n))
     return int(n)
+
+
+def decode_windows_multi(chains, latents_host, audio_host, frames: int, flags: int = 0, cancel=None) -> None:
+    """Host-to-host decode of independent windows over several chains (one per GPU) from one
+    process: chain i decodes a contiguous block of the windows on its own thread and stream."""
+    lat_ptr = latents_host.ctypes.data if hasattr(latents_host, "ctypes") else latents_host.data_ptr()
+    out_ptr = audio_host.ctypes.data if hasattr(audio_host, "ctypes") else audio_host.data_ptr()
+    handles = (ctypes.c_void_p * len(chains))(*[c.handle.value for c in chains])
+    cb = CANCEL_FN(lambda _u: 1 if cancel() else 0) if cancel is not None else CANCEL_FN()
+    check(lib().levo_vae_chains_decode_windows(ctypes.cast(handles, ctypes.c_void_p), len(chains), lat_ptr,
+                                               latents_host.shape[0], frames, out_ptr, flags, cb, None))
 
 
 class VaeChain:

@@ -286,3 +286,35 @@ def test_decode_windows_rejects_non_finite_latent(ops, dev):
     with pytest.raises(ops.LevoOpsError, match="non-finite value \\(window 1\\)"):
         chain.decode_windows(lat, out, 6)
     assert np.all(np.isfinite(out[0])) and np.all(np.isnan(out[1:]))
+
+
+@pytest.mark.parametrize("windows,n_chains", [(5, 2), (7, 3), (2, 3), (0, 2)])
+def test_chains_decode_windows_matches_single_chain(ops, dev, windows, n_chains):
+    """One-process DECODE over several chains (here all on device 0, as a box with one GPU
+    has): each window's audio equals the single-chain host decode."""
+    topo = small_topology(ops)
+    params = params_for(ops, topo, 60)
+    frames = 10
+    lat = np.random.default_rng(60).standard_normal((windows, topo.latent_dim, frames)).astype(np.float32)
+    chains = [ops.VaeChain(topo, params, max_frames=frames, device=0) for _ in range(n_chains)]
+    s = chains[0].samples(frames)
+    multi = np.full((windows, 2, s), np.nan, np.float32)
+    ops.decode_windows_multi(chains, lat, multi, frames, flags=ops.CHAIN_TANH)
+    single = np.empty((windows, 2, s), np.float32)
+    chains[0].decode_windows(lat, single, frames, flags=ops.CHAIN_TANH)
+    assert np.array_equal(multi, single)
+
+
+def test_chains_decode_windows_reports_the_failing_chain(ops, dev):
+    topo = small_topology(ops)
+    params = params_for(ops, topo, 61)
+    chains = [ops.VaeChain(topo, params, max_frames=6, device=0) for _ in range(2)]
+    lat = np.random.default_rng(61).standard_normal((4, topo.latent_dim, 6)).astype(np.float32)
+    lat[3, 0, 0] = np.nan  # window 3 belongs to chain 1 (windows 2..3)
+    out = np.empty((4, 2, chains[0].samples(6)), np.float32)
+    with pytest.raises(ops.LevoOpsError, match="non-finite.*chain 1"):
+        ops.decode_windows_multi(chains, lat, out, 6)
+    other = ops.VaeChain(small_topology(ops, residual=1), params_for(ops, small_topology(ops, residual=1), 62),
+                         max_frames=6, device=0)
+    with pytest.raises(ValueError, match="one topology"):
+        ops.decode_windows_multi([chains[0], other], lat, out, 6)
