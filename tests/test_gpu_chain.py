@@ -318,3 +318,19 @@ def test_chains_decode_windows_reports_the_failing_chain(ops, dev):
                          max_frames=6, device=0)
     with pytest.raises(ValueError, match="one topology"):
         ops.decode_windows_multi([chains[0], other], lat, out, 6)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_chains_decode_windows_across_devices(ops):
+    """One chain on each of two GPUs, reference topology: same audio as one chain on GPU 0."""
+    topo = ops.reference_topology()
+    params = params_for(ops, topo, 63)
+    frames, windows = 40, 6
+    lat = np.random.default_rng(63).standard_normal((windows, 64, frames)).astype(np.float32)
+    chains = [ops.VaeChain(topo, params, max_frames=frames, device=d) for d in (0, 1)]
+    s = chains[0].samples(frames)
+    multi = np.full((windows, 2, s), np.nan, np.float32)
+    ops.decode_windows_multi(chains, lat, multi, frames, flags=ops.CHAIN_TANH)
+    single = np.empty_like(multi)
+    chains[0].decode_windows(lat, single, frames, flags=ops.CHAIN_TANH)
+    assert np.array_equal(multi, single)
