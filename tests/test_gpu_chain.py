@@ -334,3 +334,31 @@ def test_chains_decode_windows_across_devices(ops):
     single = np.empty_like(multi)
     chains[0].decode_windows(lat, single, frames, flags=ops.CHAIN_TANH)
     assert np.array_equal(multi, single)
+
+
+def test_chain_decode_captures_into_a_cuda_graph(ops, dev):
+    """A device-resident decode records into a CUDA graph (programmatic-dependent launches
+    included) and its replay gives the eager decode's bits."""
+    topo = ops.reference_topology()
+    params = params_for(ops, topo, 64)
+    frames = 8
+    lat = torch.from_numpy(np.random.default_rng(64).standard_normal((64, frames)).astype(np.float32)).to(dev)
+    chain = ops.VaeChain(topo, params, max_frames=frames, device=0)
+    eager = torch.empty((2, chain.samples(frames)), device=dev)
+    chain.decode(lat, eager, frames, flags=ops.CHAIN_TANH)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    graphed = torch.full_like(eager, np.nan)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        chain.decode(lat, graphed, frames, flags=ops.CHAIN_TANH, stream=stream.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(graphed, eager)
+    lat.add_(0.5)  # the graph reads the latent buffer anew on every replay
+    chain.decode(lat, eager, frames, flags=ops.CHAIN_TANH)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(graphed, eager)
+    del g
+    chain.close()
