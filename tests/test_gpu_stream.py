@@ -232,3 +232,23 @@ def test_snakebeta_vector_and_scalar_paths_agree_bitwise(ops, dev, scale):
     wide[:, :t] = x
     strided = ops.snakebeta_t(wide[:, :t], a, b)  # row stride t + 3: scalar path
     assert torch.equal(dense, strided)
+
+
+def test_sin_squared_accuracy_against_float64(ops, dev):
+    """This library's sin^2 (Cody-Waite reduction + fitted polynomial, |t| <= 65536; CUDA sinf
+    beyond) against float64 sin^2 of the same F32 argument t = fl(x * alpha).  With |x| <= 1
+    and 1/beta = 1, y - x recovers sin^2(t) to within one rounding of y; the bound below is
+    4 F32 ulp at 1 (CUDA's sinf is specified to 2 ulp, so its square to about 2.4e-7)."""
+    rng = np.random.default_rng(71)
+    alphas = np.array([2.0 ** k for k in range(0, 21)] + [3.7, 1234.5, 65535.0, 70000.0], np.float32)
+    c, t = alphas.size, 65536
+    x = rng.uniform(-1, 1, (c, t)).astype(np.float32)
+    alpha = torch.from_numpy(alphas).to(dev)
+    inv_beta = torch.ones(c, device=dev)
+    y = ops.snakebeta_t(torch.from_numpy(x).to(dev), alpha, inv_beta, prepared=True).cpu().numpy()
+    targ = (x * alphas[:, None]).astype(np.float32).astype(np.float64)  # the F32 product the kernel forms
+    want = np.sin(targ) ** 2
+    got = y.astype(np.float64) - x.astype(np.float64)
+    err = np.abs(got - want)
+    assert err.max() <= 4 * 2.0 ** -23, f"max |sin^2 error| {err.max():.3g}"
+    assert (np.abs(targ) > 65536).any() and (np.abs(targ) < 65536).any()  # both paths exercised
