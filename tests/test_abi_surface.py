@@ -144,3 +144,17 @@ def test_missing_library_fails_loudly(tmp_path):
     )
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
     assert "raised" in out.stdout and "missing" in out.stdout, out.stdout + out.stderr
+
+
+@pytest.mark.parametrize("lang,header,std", [("c", "levo_ops.h", "-std=c99"), ("c++", "levo_ops.hpp", "-std=c++17")])
+def test_headers_compile_standalone(lang, header, std):
+    """levo_ops.h is plain C99 (a cgo / ctypes / JNI binding can include it); levo_ops.hpp is C++17."""
+    import shutil
+    import subprocess
+
+    compiler = shutil.which("gcc" if lang == "c" else "g++")
+    if compiler is None:
+        pytest.skip("no host compiler")
+    out = subprocess.run([compiler, std, "-Wall", "-Wextra", "-Werror", "-pedantic", "-fsyntax-only", "-x", lang,
+                          str(ROOT / "include" / header)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
