@@ -157,7 +157,9 @@ __device__ __forceinline__ float snake_inv_beta_param(const void *p, int64_t c, 
 // sin(t)^2, written for this library (no sinf call on the common path):
 //  1. Cody-Waite argument reduction (W. J. Cody, W. Waite, "Software Manual for
 //     the Elementary Functions", 1980): k = rint(t * 2/pi), r = t - k*pi/2 with
-//     pi/2 split into three F32 parts applied by FMA; |r| <= pi/4.  k is rounded
+//     pi/2 split into two F32 parts applied by FMA; |r| <= pi/4.  (The third
+//     part, -1.78e-15, would move r by at most |k| * 1.8e-15 <= 7.5e-11 for
+//     |t| <= 65536: below 0.01 ulp of sin^2 in absolute terms.)  k is rounded
 //     by adding 1.5*2^23 (the sum's ulp is 1, so the FMA rounds t*2/pi to the
 //     nearest integer) and its parity is the sum's lowest mantissa bit.
 //  2. sin(t)^2 = sin(r)^2 for even k and 1 - sin(r)^2 for odd k.
@@ -171,9 +173,8 @@ constexpr float kSin2FastLimit = 65536.0f;
 // The constants of the three steps above (shared by the scalar and paired forms).
 constexpr float kSin2Big = 12582912.0f;                 // 1.5 * 2^23
 constexpr float kSin2TwoOverPi = 0.636619747f;
-constexpr float kSin2PiOver2A = 1.57079637f;  // pi/2 = A + B + C
+constexpr float kSin2PiOver2A = 1.57079637f;  // pi/2 = A + B (+ 1.8e-15)
 constexpr float kSin2PiOver2B = -4.37113883e-08f;
-constexpr float kSin2PiOver2C = -1.77635684e-15f;
 constexpr float kSin2Q0 = -4.103582341e-06f;  // Q(z) = ((((Q0 z + Q1) z + Q2) z + Q3) z + Q4) z + Q5
 constexpr float kSin2Q1 = 1.409736724e-04f;
 constexpr float kSin2Q2 = -3.174564568e-03f;
@@ -189,7 +190,6 @@ __device__ __forceinline__ float sin_squared_fast(float t) {
     const float k = __fadd_rn(ks, -kSin2Big);
     float r = __fmaf_rn(k, -kSin2PiOver2A, t);
     r = __fmaf_rn(k, -kSin2PiOver2B, r);
-    r = __fmaf_rn(k, -kSin2PiOver2C, r);
     const float z = __fmul_rn(r, r);
     float q = __fmaf_rn(z, kSin2Q0, kSin2Q1);
     q = __fmaf_rn(q, z, kSin2Q2);
@@ -213,7 +213,6 @@ __device__ __forceinline__ float2 sin_squared_fast2(float2 t) {
     const float2 k = __fadd2_rn(ks, pair(-kSin2Big));
     float2 r = __ffma2_rn(k, pair(-kSin2PiOver2A), t);
     r = __ffma2_rn(k, pair(-kSin2PiOver2B), r);
-    r = __ffma2_rn(k, pair(-kSin2PiOver2C), r);
     const float2 z = __fmul2_rn(r, r);
     float2 q = __ffma2_rn(z, pair(kSin2Q0), pair(kSin2Q1));
     q = __ffma2_rn(q, z, pair(kSin2Q2));
