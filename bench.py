@@ -375,6 +375,12 @@ def kernel_suite(ops, dev, peak, steps, warmup):
         ms = timeit(lambda: dst.copy_(src))
         out[f"torch_copy_{mb}MB_reference"] = {"ms": ms, "GB/s": 2 * src.numel() * 4 / (ms * 1e-3) / 1e9,
                                               "frac": 2 * src.numel() * 4 / (ms * 1e-3) / 1e9 / peak}
+    # The ~13-60 MB kernels against what a plain device copy of ~50 MB reaches (launch, ramp-up and one
+    # DRAM round trip dominate at that size): GB/s of the kernel / GB/s of that copy.
+    copy_gbs = out["torch_copy_50MB_reference"]["GB/s"]
+    for name in ("add_rmsnorm_f16[4096,1536]", "add_layernorm_f16[4096,1536]", "weightnorm_f32[1024,7168]",
+                 "cfg_euler_f32[2,64,252]x50"):
+        out[name]["of_50MB_copy"] = out[name]["GB/s"] / copy_gbs
     return out
 
 
