@@ -79,14 +79,18 @@ def test_reference_topology_matches_oracle(ops, orc, dev, frames):
     assert_close(audio.cpu().numpy(), oracle_audio(orc, topo, params, latent, frames), TOL)
 
 
-@pytest.mark.parametrize("frames,tanh", [(252, False), (750, True)])
-def test_reference_topology_full_window_matches_oracle(ops, orc, dev, frames, tanh):
+@pytest.mark.parametrize("frames,tanh,f16", [(252, False, False), (750, True, False), (750, True, True)])
+def test_reference_topology_full_window_matches_oracle(ops, orc, dev, frames, tanh, f16):
     """BASELINE config 3 (one 10.08 s window, T = 252, final [128][483840] stage) and one
-    config-4 window (T = 750 with the tanh epilogue) at full size against the oracle."""
+    config-4 window (T = 750 with the tanh epilogue; F32- and F16-stored parameters, the
+    latter promoted in-kernel) at full size against the oracle."""
     topo = ops.reference_topology()
     params = params_for(ops, topo, 13)
+    if f16:
+        params = params.astype(np.float16)
     latent = np.random.default_rng(frames).standard_normal((64, frames)).astype(np.float32)
     chain = ops.VaeChain(topo, params, max_frames=frames, device=0)
+    params = params.astype(np.float32)  # the oracle takes the promoted values
     audio = torch.empty((2, frames * 1920), device=dev)
     chain.decode(torch.from_numpy(latent).to(dev), audio, frames, flags=ops.CHAIN_TANH if tanh else 0)
     assert_close(audio.cpu().numpy(), oracle_audio(orc, topo, params, latent, frames, tanh), TOL)

@@ -168,6 +168,22 @@ def test_gated_layernorm_modulate_matches_oracle(ops, orc, dev, dim, parts):
     assert_close(y.cpu().numpy(), yw, 1e-5, parts)
 
 
+def test_gated_layernorm_modulate_flow_full_size(ops, orc, dev):
+    # The Flow estimator's real block size: [batch = 2 (CFG rows)][1000 frames][2200] F32.
+    rng = np.random.default_rng(2200)
+    batch, frames, dim = 2, 1000, 2200
+    rows = batch * frames
+    x, r = rng.standard_normal((2, rows, dim)).astype(np.float32)
+    gate, scale, shift = (0.5 * rng.standard_normal((3, batch, dim))).astype(np.float32)
+    gamma = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    beta = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+    T = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+    h, y = ops.gated_layernorm_modulate_t(T(x), T(gate), T(r), T(gamma), T(beta), T(scale), T(shift), frames)
+    hw, yw = orc.gated_layernorm_modulate(x, gate, r, gamma, beta, scale, shift, frames)
+    assert np.array_equal(h.cpu().numpy(), hw)
+    assert_close(y.cpu().numpy(), yw, 1e-5, "flow full size")
+
+
 def test_gated_layernorm_modulate_rejects_bad_batch(ops, dev):
     x = torch.zeros((10, 64), device=dev)
     g = torch.ones(64, device=dev)
