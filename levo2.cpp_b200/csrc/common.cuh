@@ -25,6 +25,11 @@ void clear_error();
 int check_launch(const char *what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Resident CTAs per SM of `kernel` at this block size and dynamic shared
+// memory on the current device, opting the kernel in to more than 48 KB of
+// shared memory when needed.  Both are done once per (kernel, device, size) and
+// cached, not on every launch.
+cudaError_t resident_ctas(const void *kernel, int threads, size_t smem_bytes, int *per_sm);
 
 inline bool aligned_to(const void *p, uintptr_t bytes) {
     return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;

@@ -606,16 +606,13 @@ int run_norm(const char *what, const void *x, const void *r, const float *gamma,
             if (m && !aligned_to(m, 16)) staged = false;
         if (staged) {
             auto kernel = add_norm_staged_kernel<T, LAYER, MOD>;
-            if (smem > 48 * 1024 &&
-                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)) != cudaSuccess)
+            int per_sm = 0;
+            if (resident_ctas(reinterpret_cast<const void *>(kernel), kStagedRows * 32, smem, &per_sm) !=
+                cudaSuccess) {
+                cudaGetLastError();  // clear the failed opt-in; fall back to the register form
                 staged = false;
+            }
             if (staged) {
-                int per_sm = 0;
-                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kStagedRows * 32, smem) !=
-                        cudaSuccess ||
-                    per_sm <= 0)
-                    per_sm = 1;
                 const int64_t grid = std::min<int64_t>((rows + kStagedRows - 1) / kStagedRows,
                                                        static_cast<int64_t>(sm_count()) * per_sm);
                 kernel<<<static_cast<unsigned>(grid), kStagedRows * 32, smem, stream>>>(a);

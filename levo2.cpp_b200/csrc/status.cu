@@ -2,8 +2,12 @@
 // Mirrors the reference's thread-local last-error pair
 // (src/cantor-abi.cpp:55-66): each failing call stores a message that
 // levo_ops_last_error() returns on the same thread.
+#include <algorithm>
 #include <atomic>
+#include <map>
+#include <mutex>
 #include <string>
+#include <tuple>
 
 #include "common.cuh"
 
@@ -39,6 +43,39 @@ int sm_count() {
         count = 148;
     g_sm_count[device].store(count, std::memory_order_relaxed);
     return count;
+}
+
+cudaError_t resident_ctas(const void *kernel, int threads, size_t smem_bytes, int *per_sm) {
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return err;
+    static std::mutex mu;
+    static std::map<std::tuple<const void *, int, int, size_t>, int> occupancy;  // (kernel, device, threads, smem)
+    static std::map<std::pair<const void *, int>, size_t> opted;                  // (kernel, device) -> smem
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(kernel, device, threads, smem_bytes);
+    const auto hit = occupancy.find(key);
+    if (hit != occupancy.end()) {
+        *per_sm = hit->second;
+        return cudaSuccess;
+    }
+    if (smem_bytes > 48 * 1024) {
+        // the opt-in only ever grows, so an earlier, larger launch of this kernel stays valid
+        size_t &limit = opted[std::make_pair(kernel, device)];
+        if (limit < smem_bytes) {
+            err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem_bytes));
+            if (err != cudaSuccess) return err;
+            limit = smem_bytes;
+        }
+    }
+    int n = 0;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem_bytes);
+    if (err != cudaSuccess) return err;
+    n = std::max(n, 1);
+    occupancy.emplace(key, n);
+    *per_sm = n;
+    return cudaSuccess;
 }
 
 }  // namespace levo

@@ -316,11 +316,11 @@ template <bool HAS_RES, bool SNAKE>
 int launch_variant(const StreamArgs &a, bool vec, size_t smem_bytes, cudaStream_t stream,
                    const char *what) {
     auto kernel = vec ? stream_vec8_kernel<HAS_RES, SNAKE> : stream_scalar_kernel<HAS_RES, SNAKE>;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem_bytes) !=
-            cudaSuccess ||
-        per_sm <= 0)
+    int per_sm = 1;
+    if (resident_ctas(reinterpret_cast<const void *>(kernel), kThreads, smem_bytes, &per_sm) != cudaSuccess) {
+        cudaGetLastError();
         per_sm = 1;
+    }
     const int64_t work_items = vec ? (a.nvec + kUnroll - 1) / kUnroll : a.n;
     const int64_t needed = std::max<int64_t>(1, (work_items + kThreads - 1) / kThreads);
     // vector form: one CTA per tile, as in the rows form; scalar form: persistent grid

@@ -366,3 +366,21 @@ def test_chain_decode_captures_into_a_cuda_graph(ops, dev):
     assert torch.equal(graphed, eager)
     del g
     chain.close()
+
+
+def test_chains_decode_windows_cancellation(ops, dev):
+    # The cancel callback is polled by every chain's thread before each of its windows.
+    topo = small_topology(ops)
+    params = params_for(ops, topo, 65)
+    chains = [ops.VaeChain(topo, params, max_frames=6, device=0) for _ in range(2)]
+    lat = np.random.default_rng(65).standard_normal((6, topo.latent_dim, 6)).astype(np.float32)
+    out = np.empty((6, 2, chains[0].samples(6)), np.float32)
+    polls = []
+
+    def cancel():
+        polls.append(1)
+        return len(polls) > 3
+
+    with pytest.raises(ops.LevoCancelled, match="chain"):
+        ops.decode_windows_multi(chains, lat, out, 6, cancel=cancel)
+    assert len(polls) >= 4
