@@ -109,6 +109,8 @@ def test_zero_sizes_are_noops_without_gpu(ops):
     assert lib.levo_weightnorm_f32(p, p, p, None, 0, 7, None) == ops.OK
     assert lib.levo_snake_params_prepare(p, p, 0, 0, p, p, None) == ops.OK
     assert lib.levo_vae_chain_set_stage_capture(None, None, 0) == ops.EINVAL  # no chain
+    assert lib.levo_vae_chains_decode_windows(None, 0, p, 1, 1, p, 0, ops.CANCEL_FN(), None) == ops.EINVAL
+    assert lib.levo_snake_params_prepare(p, p, 0, 0, p, p, None) == ops.OK
 
 
 def test_chain_rejects_bad_topology_without_gpu(ops):
