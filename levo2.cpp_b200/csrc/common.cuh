@@ -267,6 +267,15 @@ __device__ __forceinline__ void snake_eval8(float (&v)[8], float alpha, float in
     }
 }
 
+// Block b's share [begin, end) of `items` split over the grid in contiguous
+// ranges whose sizes differ by at most one (quotient and remainder: no
+// items * blockIdx product that could overflow for huge tensors).
+__device__ __forceinline__ void block_range(int64_t items, int64_t &begin, int64_t &end) {
+    const int64_t per = items / gridDim.x, extra = items % gridDim.x, b = blockIdx.x;
+    begin = per * b + (b < extra ? b : extra);
+    end = begin + per + (b < extra ? 1 : 0);
+}
+
 // ---------------------------------------------------------------------------
 // Flat index -> row (channel) of a dense [rows][len] tensor.  The quotient is
 // estimated in double (exact for e < 2^53) and corrected by one step.

@@ -116,7 +116,7 @@ __device__ __forceinline__ void unit_eval8(const StreamArgs &a, const ChannelPar
     }
 }
 
-// Rows form: CTA b owns chunks [b*chunks/G, (b+1)*chunks/G); chunk q covers
+// Rows form: CTA b owns a contiguous share of the chunks (block_range); chunk q covers
 // vectors [k*kRowThreads*UNROLL, (k+1)*kRowThreads*UNROLL) of row c, q = c*cpr + k.
 // Short-lived CTAs that the block scheduler refills keep HBM busier than a
 // persistent grid (a plain 2-in/2-out stream on B200: ~6.8 against ~6.0 TB/s),
@@ -126,8 +126,8 @@ template <bool HAS_RES, bool SNAKE, int UNROLL, bool RAGGED>
 __global__ void __launch_bounds__(kRowThreads) stream_rows_kernel(const StreamArgs a) {
     pdl_wait();
     pdl_trigger();
-    const int64_t q0 = a.chunks * blockIdx.x / gridDim.x;
-    const int64_t q1 = a.chunks * (blockIdx.x + 1) / gridDim.x;
+    int64_t q0, q1;
+    block_range(a.chunks, q0, q1);
     if (q0 >= q1) return;
     int64_t c = row_of(q0, a.chunks_per_row, a.inv_chunks_per_row);
     int64_t k = q0 - c * a.chunks_per_row;
@@ -223,8 +223,8 @@ __global__ void __launch_bounds__(kThreads) stream_vec8_kernel(const StreamArgs 
     // changes rarely; its parameters are cached in registers by channel.
     const int64_t tile_vecs = static_cast<int64_t>(kThreads) * kUnroll;
     const int64_t tiles = (a.nvec + tile_vecs - 1) / tile_vecs;
-    const int64_t t0 = tiles * blockIdx.x / gridDim.x;
-    const int64_t t1 = tiles * (blockIdx.x + 1) / gridDim.x;
+    int64_t t0, t1;
+    block_range(tiles, t0, t1);
     int64_t cached_c = -1;
     ChannelParams cached{};
     auto params_for = [&](int64_t c) -> ChannelParams {
