@@ -365,7 +365,9 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
     const MultiArgs a{state, noise, context, uncond, cond, batch, row, prefix, first_step,
                       count, steps, cfg ? 1 : 0, guidance, sigma_min, status};
     const int64_t n = batch * row;
-    const bool staged = count > 0 && n % 4 == 0 && aligned_to(uncond, 16) && (!cfg || aligned_to(cond, 16));
+    // one staged CTA per kStagedThreads elements: the grid must fit in 2^31 - 1 blocks
+    const bool staged = count > 0 && n % 4 == 0 && aligned_to(uncond, 16) && (!cfg || aligned_to(cond, 16)) &&
+                        (n + kStagedThreads - 1) / kStagedThreads <= 0x7fffffff;
     if (staged) {
         // [2][kStagedSteps][kStagedThreads] F32 = 32 KB of shared memory
         const size_t smem = 2 * kStagedSteps * kStagedThreads * sizeof(float);

@@ -79,8 +79,9 @@ LEVO_OPS_API int levo_latent_to_vae_f32(const float *frame_major, const float *m
     if (rc != LEVO_OPS_OK) return rc;
     if (frame_major == channel_major)
         return set_error(LEVO_OPS_EINVAL, std::string(w) + ": the transpose cannot run in place");
+    if ((dim + kTile - 1) / kTile > 65535 || (frames + kTile - 1) / kTile > 0x7fffffff)
+        return set_error(LEVO_OPS_EUNSUPPORTED, std::string(w) + ": latent too large for one launch");
     const dim3 grid(static_cast<unsigned>((frames + kTile - 1) / kTile), static_cast<unsigned>((dim + kTile - 1) / kTile));
-    if (grid.y > 65535) return set_error(LEVO_OPS_EUNSUPPORTED, std::string(w) + ": latent dim too large");
     denorm_transpose_kernel<<<grid, dim3(kTile, 8), 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         frame_major, mean, stddev, frames, dim, channel_major, denorm ? 1 : 0);
     return check_launch(w);
