@@ -44,28 +44,33 @@ class HostGather:
         self.shm = None
         self.path = None
         # POSIX shared memory when /dev/shm has room, else a file mapping in the temp dir.
-        use_shm = _free_bytes("/dev/shm") > self.nbytes * 1.1
-        if use_shm:
-            if rank == 0:
-                try:
-                    stale = shared_memory.SharedMemory(name=self.name)
-                    stale.close()
-                    stale.unlink()
-                except FileNotFoundError:
-                    pass
+        # Rank 0 decides (and clears stale segments or files of the same name); the others
+        # attach to whichever it created, so all ranks agree even when /dev/shm is nearly full.
+        file_path = os.path.join(tempfile.gettempdir(), self.name + ".f32")
+        if rank == 0:
+            try:
+                stale = shared_memory.SharedMemory(name=self.name)
+                stale.close()
+                stale.unlink()
+            except FileNotFoundError:
+                pass
+            if os.path.exists(file_path):
+                os.unlink(file_path)
+            if _free_bytes("/dev/shm") > self.nbytes * 1.1:
                 self.shm = shared_memory.SharedMemory(name=self.name, create=True, size=self.nbytes)
-            barrier()
-            if rank != 0:
+            else:
+                self.path = file_path
+                self.array = np.memmap(self.path, dtype=np.float32, mode="w+", shape=self.shape)
+        barrier()
+        if rank != 0:
+            try:
                 self.shm = shared_memory.SharedMemory(name=self.name)
                 _untrack(self.shm)
-            self.array = np.ndarray(self.shape, dtype=np.float32, buffer=self.shm.buf)
-        else:
-            self.path = os.path.join(tempfile.gettempdir(), self.name + ".f32")
-            if rank == 0:
-                self.array = np.memmap(self.path, dtype=np.float32, mode="w+", shape=self.shape)
-            barrier()
-            if rank != 0:
+            except FileNotFoundError:
+                self.path = file_path
                 self.array = np.memmap(self.path, dtype=np.float32, mode="r+", shape=self.shape)
+        if self.shm is not None:
+            self.array = np.ndarray(self.shape, dtype=np.float32, buffer=self.shm.buf)
 
     def view(self, start: int, stop: int) -> np.ndarray:
         return self.array[start:stop]

@@ -38,12 +38,14 @@ def fake_decode(window: int, shape) -> np.ndarray:
     return np.full(shape, float(window + 1), np.float32) * np.arange(shape[-1], dtype=np.float32)
 
 
-def _worker(rank, world, port, tag, windows, fail_rank, q):
+def _worker(rank, world, port, tag, windows, fail_rank, force_file, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     sh = entry.load_package().sharding
+    if force_file and rank == 0:
+        sh._free_bytes = lambda _path: 0  # rank 0 alone sees a full /dev/shm: the others must follow it
     try:
         shape = (windows, 2, 50)
         g = sh.HostGather(tag, shape, rank, dist.barrier)
@@ -63,6 +65,7 @@ def _worker(rank, world, port, tag, windows, fail_rank, q):
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         elapsed = torch.tensor([0.5 + rank], dtype=torch.float64)
         dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+        assert (g.shm is None) == force_file
         if rank == 0:
             complete = bool(flag.item())
             good = complete and all(np.array_equal(g.array[w], fake_decode(w, shape[1:])) for w in range(windows))
@@ -72,13 +75,14 @@ def _worker(rank, world, port, tag, windows, fail_rank, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fail_rank", [-1, 1])
-def test_two_rank_gather(fail_rank):
+@pytest.mark.parametrize("fail_rank,force_file", [(-1, False), (1, False), (-1, True)])
+def test_two_rank_gather(fail_rank, force_file):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     tag = f"test_{port}"
-    mp.start_processes(_worker, args=(2, port, tag, 7, fail_rank, q), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(2, port, tag, 7, fail_rank, force_file, q), nprocs=2, join=True,
+                       start_method="spawn")
     complete, good, elapsed = q.get(timeout=10)
     assert elapsed == 1.5  # max over ranks
     if fail_rank < 0:
