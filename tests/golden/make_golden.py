@@ -1,8 +1,8 @@
 """Generates the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container where the reference tree exists (default /root/reference,
-override with LEVO_REFERENCE_ROOT) after `make -C oracle` has built
-oracle/_ref/libref_levo.so:
+Run where the reference tree exists (its path in LEVO_REFERENCE_ROOT, or the
+default checkout location the oracle Makefile also uses) after `make -C oracle`
+has built oracle/_ref/libref_levo.so:
 
     python tests/golden/make_golden.py
 
