@@ -22,6 +22,15 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and liblevo_b200.so")
 
 
+def pytest_sessionstart(session):
+    """A fresh checkout has neither liblevo_b200.so nor the oracle library: build them once
+    (nvcc and gcc).  Existing builds are used as they are."""
+    lib = ROOT / "levo2.cpp_b200" / "liblevo_b200.so"
+    oracle_lib = ROOT / "oracle" / "liblevo_oracle.so"
+    if not lib.exists() or not oracle_lib.exists():
+        entry.build()
+
+
 @pytest.fixture(scope="session")
 def pkg():
     return entry.load_package()
