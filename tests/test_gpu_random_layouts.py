@@ -1,0 +1,75 @@
+"""Seeded random sweep over shapes and memory layouts of the streaming kernels, against the
+oracle.  Random element offsets into larger buffers give every dispatch path: rows form
+(all tensors 32-byte aligned, rows a multiple of 8 long), ragged rows (aligned, other
+lengths), the flat vector form (one common nonzero 32-byte phase) and the scalar form
+(mismatched phases, or row strides).  Tolerance 1e-5 scaled; x (sums only) bit-exact."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def placed(dev, arr, offset):
+    """A CUDA view of `arr` starting `offset` floats into a fresh 256-byte aligned buffer."""
+    buf = torch.empty(arr.size + offset + 8, dtype=torch.float32, device=dev)
+    view = buf[offset:offset + arr.size].view(arr.shape)
+    view.copy_(torch.from_numpy(arr))
+    return view
+
+
+def empty_placed(dev, shape, offset):
+    n = int(np.prod(shape))
+    buf = torch.full((n + offset + 8,), np.nan, dtype=torch.float32, device=dev)
+    return buf[offset:offset + n].view(shape)
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_fused_unit_random_layouts(ops, orc, dev, seed):
+    rng = np.random.default_rng(1000 + seed)
+    c = int(rng.integers(1, 200))
+    t = int(rng.choice([int(rng.integers(1, 64)), int(rng.integers(64, 3000)), 8 * int(rng.integers(8, 400))]))
+    mode = rng.choice(["aligned", "common_phase", "mixed"])
+    if mode == "aligned":
+        offs = [0, 0, 0, 0]
+    elif mode == "common_phase":
+        offs = [int(rng.integers(1, 8))] * 4
+    else:
+        offs = [int(o) for o in rng.integers(0, 8, 4)]
+    has_res, has_bias, snake, write_x, tanh = (bool(b) for b in rng.integers(0, 2, 5))
+    u = rng.standard_normal((c, t)).astype(np.float32)
+    r = rng.standard_normal((c, t)).astype(np.float32) if has_res else None
+    b = (0.05 * rng.standard_normal(c)).astype(np.float32) if has_bias else None
+    al, bl = ((0.3 * rng.standard_normal((2, c))).astype(np.float32) if snake else (None, None))
+    tu = placed(dev, u, offs[0])
+    tr = placed(dev, r, offs[1]) if has_res else None
+    x_out = empty_placed(dev, (c, t), offs[2]) if write_x else None
+    y_out = empty_placed(dev, (c, t), offs[3])
+    g = lambda a: None if a is None else torch.from_numpy(a).to(dev)  # noqa: E731
+    ops.fused_unit_t(tu, g(b), tr, g(al), g(bl), x_out, y_out, tanh=tanh)
+    xw, yw = orc.fused_unit(u, b, r, al, bl, tanh=tanh)
+    what = f"c={c} t={t} mode={mode} offs={offs} res={has_res} bias={has_bias} snake={snake} tanh={tanh}"
+    assert_close(y_out.cpu().numpy(), yw, TOL, what)
+    if write_x:
+        assert np.array_equal(x_out.cpu().numpy(), xw), what
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_snakebeta_random_strides(ops, orc, dev, seed):
+    rng = np.random.default_rng(2000 + seed)
+    c, t = int(rng.integers(1, 100)), int(rng.integers(1, 4000))
+    pad_x, pad_y = (int(p) for p in rng.integers(0, 17, 2))
+    x = rng.standard_normal((c, t)).astype(np.float32)
+    al, bl = (0.3 * rng.standard_normal((2, c))).astype(np.float32)
+    wide_x = torch.empty((c, t + pad_x), device=dev)
+    wide_x[:, :t] = torch.from_numpy(x).to(dev)
+    wide_y = torch.full((c, t + pad_y), np.nan, device=dev)
+    ops.snakebeta_t(wide_x[:, :t], torch.from_numpy(al).to(dev), torch.from_numpy(bl).to(dev), out=wide_y[:, :t])
+    assert_close(wide_y[:, :t].cpu().numpy(), orc.snakebeta(x, al, bl), TOL, f"c={c} t={t} pads={pad_x},{pad_y}")
+    if pad_y:
+        assert torch.isnan(wide_y[:, t:]).all()  # nothing written past each row
