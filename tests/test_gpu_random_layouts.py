@@ -1,5 +1,5 @@
-"""Seeded random sweep over shapes and memory layouts of the streaming kernels, against the
-oracle.  Random element offsets into larger buffers give every dispatch path: rows form
+"""Seeded random sweep over shapes and memory layouts of the streaming and norm kernels,
+against the oracle.  Random element offsets into larger buffers give every dispatch path: rows form
 (all tensors 32-byte aligned, rows a multiple of 8 long), ragged rows (aligned, other
 lengths), the flat vector form (one common nonzero 32-byte phase) and the scalar form
 (mismatched phases, or row strides).  Tolerance 1e-5 scaled; x (sums only) bit-exact."""
@@ -73,3 +73,45 @@ def test_snakebeta_random_strides(ops, orc, dev, seed):
     assert_close(wide_y[:, :t].cpu().numpy(), orc.snakebeta(x, al, bl), TOL, f"c={c} t={t} pads={pad_x},{pad_y}")
     if pad_y:
         assert torch.isnan(wide_y[:, t:]).all()  # nothing written past each row
+
+
+def placed_dtype(dev, arr, offset, dtype):
+    buf = torch.empty(arr.size + offset + 16, dtype=dtype, device=dev)
+    view = buf[offset:offset + arr.size].view(arr.shape)
+    view.copy_(torch.from_numpy(arr))
+    return view
+
+
+@pytest.mark.parametrize("seed", range(30))
+def test_add_norm_random_layouts(ops, orc, dev, seed):
+    """Random dims, row counts, F16 / F32, residual or none, the F16-boundary flag and element
+    offsets (16-byte aligned rows take the staged form, others the register or scalar form)."""
+    rng = np.random.default_rng(3000 + seed)
+    layer = bool(rng.integers(0, 2))
+    half = bool(rng.integers(0, 2))
+    npdt, tdt = (np.float16, torch.float16) if half else (np.float32, torch.float32)
+    dim = int(rng.choice([int(rng.integers(1, 64)), int(rng.integers(64, 5000)), 8 * int(rng.integers(1, 700))]))
+    rows = int(rng.integers(1, 300))
+    with_r = bool(rng.integers(0, 4))  # mostly with a residual
+    boundary = half and bool(rng.integers(0, 2))
+    off = 0 if rng.integers(0, 2) else int(rng.integers(1, 8))
+    x = rng.standard_normal((rows, dim)).astype(npdt)
+    r = rng.standard_normal((rows, dim)).astype(npdt) if with_r else None
+    g = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+    eps = 1e-5
+    tx = placed_dtype(dev, x, off, tdt)
+    tr = placed_dtype(dev, r, off, tdt) if with_r else None
+    h_out = placed_dtype(dev, np.zeros((rows, dim), npdt), off, tdt) if with_r else None
+    y_out = placed_dtype(dev, np.zeros((rows, dim), npdt), off, tdt)
+    T = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+    if layer:
+        ops.add_layernorm_t(tx, tr, T(g), T(b), eps, f16_boundary=boundary, h_out=h_out, y_out=y_out)
+        hw, yw = orc.add_layernorm(x, r, g, b, eps, f16_boundary=boundary)
+    else:
+        ops.add_rmsnorm_t(tx, tr, T(g), eps, f16_boundary=boundary, h_out=h_out, y_out=y_out)
+        hw, yw = orc.add_rmsnorm(x, r, g, eps, f16_boundary=boundary)
+    what = f"layer={layer} half={half} rows={rows} dim={dim} res={with_r} boundary={boundary} off={off}"
+    if with_r:
+        assert np.array_equal(h_out.cpu().numpy(), hw), what
+    assert_close(y_out.cpu().numpy().astype(np.float64), yw.astype(np.float64), 2e-3 if half else 1e-5, what)
