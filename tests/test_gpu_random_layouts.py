@@ -1,8 +1,9 @@
-"""Seeded random sweep over shapes and memory layouts of the streaming and norm kernels,
-against the oracle.  Random element offsets into larger buffers give every dispatch path: rows form
+"""Seeded random sweep over shapes and memory layouts of the streaming, norm, weight-norm and
+CFG+Euler kernels, against the oracle.  Random element offsets into larger buffers give every dispatch path: rows form
 (all tensors 32-byte aligned, rows a multiple of 8 long), ragged rows (aligned, other
 lengths), the flat vector form (one common nonzero 32-byte phase) and the scalar form
-(mismatched phases, or row strides).  Tolerance 1e-5 scaled; x (sums only) bit-exact."""
+(mismatched phases, or row strides).  Tolerance 1e-5 scaled (norms in F16: 2e-3); x and h
+(sums only) and the Euler state bit-exact."""
 from __future__ import annotations
 
 import numpy as np
@@ -115,3 +116,50 @@ def test_add_norm_random_layouts(ops, orc, dev, seed):
     if with_r:
         assert np.array_equal(h_out.cpu().numpy(), hw), what
     assert_close(y_out.cpu().numpy().astype(np.float64), yw.astype(np.float64), 2e-3 if half else 1e-5, what)
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_weightnorm_random_layouts(ops, orc, dev, seed):
+    rng = np.random.default_rng(4000 + seed)
+    rows = int(rng.integers(1, 300))
+    cols = int(rng.choice([int(rng.integers(1, 40)), int(rng.integers(40, 13000)), 4 * int(rng.integers(1, 4000))]))
+    off = 0 if rng.integers(0, 2) else int(rng.integers(1, 8))
+    v = (0.02 * rng.standard_normal((rows, cols))).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, rows).astype(np.float32)
+    tv = placed(dev, v, off)
+    w = empty_placed(dev, (rows, cols), off)
+    ops.weightnorm_t(tv, torch.from_numpy(g).to(dev), w=w)
+    want, _, ok = orc.weightnorm(v, g)
+    assert ok
+    assert_close(w.cpu().numpy(), want, TOL, f"rows={rows} cols={cols} off={off}")
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_cfg_euler_random_schedules(ops, orc, dev, seed):
+    """Random batch / row / prefix, resume points and step counts (past one 64-step staging
+    chunk), with and without CFG: bit-exact with the oracle."""
+    rng = np.random.default_rng(5000 + seed)
+    batch = int(rng.integers(1, 4))
+    row = int(rng.choice([64 * int(rng.integers(1, 40)), int(rng.integers(1, 3000))]))
+    steps = int(rng.integers(1, 90))
+    first = int(rng.integers(0, steps))
+    count = int(rng.integers(1, steps - first + 1))
+    prefix = int(rng.integers(0, row + 1)) if rng.integers(0, 2) else 0
+    cfg = bool(rng.integers(0, 2))
+    guidance = float(rng.uniform(0.5, 3.0))
+    n = batch * row
+    x = rng.standard_normal(n).astype(np.float32)
+    noise = rng.standard_normal(n).astype(np.float32)
+    ctx = rng.standard_normal(n).astype(np.float32)
+    vu, vc = rng.standard_normal((2, count, n)).astype(np.float32)
+    T = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+    st = T(x)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.cfg_euler_multi_t(st, T(noise), T(ctx), T(vu), T(vc) if cfg else None, batch=batch, prefix=prefix,
+                          first_step=first, count=count, steps=steps, cfg=cfg, guidance=guidance, sigma_min=1e-4,
+                          status=status)
+    want, ok = orc.cfg_euler(x, noise, ctx, vu, vc if cfg else None, batch=batch, prefix=prefix, first_step=first,
+                             count=count, steps=steps, cfg=cfg, guidance=guidance, sigma_min=1e-4)
+    what = f"batch={batch} row={row} steps={steps} first={first} count={count} prefix={prefix} cfg={cfg}"
+    assert ok and status.item() == 0, what
+    assert np.array_equal(st.cpu().numpy(), want), what
