@@ -1,9 +1,9 @@
-"""Seeded random sweep over shapes and memory layouts of the streaming, norm, weight-norm and
-CFG+Euler kernels, against the oracle.  Random element offsets into larger buffers give every dispatch path: rows form
-(all tensors 32-byte aligned, rows a multiple of 8 long), ragged rows (aligned, other
-lengths), the flat vector form (one common nonzero 32-byte phase) and the scalar form
-(mismatched phases, or row strides).  Tolerance 1e-5 scaled (norms in F16: 2e-3); x and h
-(sums only) and the Euler state bit-exact."""
+"""Seeded random sweep over shapes and memory layouts of the streaming, norm, weight-norm
+and CFG+Euler kernels, against the oracle.  Random element offsets into larger buffers
+give every dispatch path: rows form (all tensors 32-byte aligned, rows a multiple of 8
+long), ragged rows (aligned, other lengths), the flat vector form (one common nonzero
+32-byte phase) and the scalar form (mismatched phases, or row strides).  Tolerance 1e-5
+scaled (norms in F16: 2e-3); x and h (sums only) and the Euler state bit-exact."""
 from __future__ import annotations
 
 import numpy as np
