@@ -1,9 +1,10 @@
-"""Seeded random sweep over shapes and memory layouts of the streaming, norm, weight-norm
-and CFG+Euler kernels, against the oracle.  Random element offsets into larger buffers
-give every dispatch path: rows form (all tensors 32-byte aligned, rows a multiple of 8
-long), ragged rows (aligned, other lengths), the flat vector form (one common nonzero
-32-byte phase) and the scalar form (mismatched phases, or row strides).  Tolerance 1e-5
-scaled (norms in F16: 2e-3); x and h (sums only) and the Euler state bit-exact."""
+"""Seeded random sweeps over shapes, memory layouts and options of every kernel family,
+against the oracle.  Random element offsets into larger buffers give every streaming
+dispatch path: rows form (all tensors 32-byte aligned, rows a multiple of 8 long), ragged
+rows (aligned, other lengths), the flat vector form (one common nonzero 32-byte phase) and
+the scalar form (mismatched phases, or row strides).  Tolerance 1e-5 scaled (norms in F16:
+2e-3); x and h (sums only), the Euler state, the assembled audio, the latent layouts and
+the greedy token indices bit-exact."""
 from __future__ import annotations
 
 import numpy as np
@@ -163,3 +164,57 @@ def test_cfg_euler_random_schedules(ops, orc, dev, seed):
     what = f"batch={batch} row={row} steps={steps} first={first} count={count} prefix={prefix} cfg={cfg}"
     assert ok and status.item() == 0, what
     assert np.array_equal(st.cpu().numpy(), want), what
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_assembly_random_schedules(ops, orc, dev, seed):
+    """Random valid schedules (0 or 2 <= overlap <= hop, hop + overlap <= window), planar and
+    interleaved output: bit-exact with the oracle."""
+    rng = np.random.default_rng(6000 + seed)
+    n = int(rng.integers(1, 9))
+    win = int(rng.integers(3, 400))
+    overlap = 0 if (win < 4 or rng.integers(0, 4) == 0) else int(rng.integers(2, win // 2 + 1))
+    hop = int(rng.integers(max(overlap, 1), win - overlap + 1))
+    target = int(rng.integers(0, (n - 1) * hop + win + 1))
+    channels = int(rng.integers(1, 4))
+    w = rng.standard_normal((n, channels, win)).astype(np.float32)
+    tw = torch.from_numpy(w).to(dev)
+    want = orc.assemble_windows(w, hop, overlap, target)
+    what = f"n={n} win={win} hop={hop} overlap={overlap} target={target} channels={channels}"
+    assert np.array_equal(ops.assemble_windows_t(tw, hop, overlap, target).cpu().numpy(), want), what
+    inter = ops.assemble_windows_t(tw, hop, overlap, target, interleaved=True).cpu().numpy()
+    assert np.array_equal(inter.reshape(target, channels).T, want), what
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_greedy_random_rows(ops, orc, dev, seed):
+    """Random vocab sizes, row counts, penalties, recent-token lists (with -1 padding and ids
+    past the penalty limit) and ignore lists: the same token indices as the oracle."""
+    rng = np.random.default_rng(7000 + seed)
+    rows = int(rng.integers(1, 40))
+    vocab = int(rng.integers(2, 20000))
+    x = (rng.standard_normal((rows, vocab)) * rng.uniform(0.1, 20)).astype(np.float32)
+    if rng.integers(0, 3) == 0:  # ties at the maximum
+        x[:, rng.integers(0, vocab, 8)] = x.max()
+    recent = rng.integers(-1, vocab, (rows, int(rng.integers(1, 80))))
+    ignore = rng.integers(0, vocab, int(rng.integers(1, 20))) if rng.integers(0, 2) else None
+    penalty = float(rng.choice([1.0, rng.uniform(1.0, 2.0)]))
+    limit = int(rng.integers(0, vocab + 1))
+    T = lambda a: None if a is None else torch.from_numpy(a).to(dev)  # noqa: E731
+    got = ops.greedy_tokens_t(T(x), recent=T(recent), penalty=penalty, penalty_limit=limit, ignore=T(ignore)).cpu()
+    want, ok = orc.greedy_tokens(x, recent, penalty, limit, ignore)
+    assert ok
+    assert np.array_equal(got.numpy(), want), f"rows={rows} vocab={vocab} penalty={penalty} limit={limit}"
+
+
+@pytest.mark.parametrize("seed", range(10))
+def test_latent_random_shapes(ops, orc, dev, seed):
+    rng = np.random.default_rng(8000 + seed)
+    frames, dim = int(rng.integers(1, 3000)), int(rng.integers(1, 200))
+    x = rng.standard_normal((frames, dim)).astype(np.float32)
+    mean = rng.standard_normal(dim).astype(np.float32)
+    std = rng.uniform(0.5, 2.0, dim).astype(np.float32)
+    T = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+    assert np.array_equal(ops.latent_to_vae_t(T(x), T(mean), T(std)).cpu().numpy(), orc.latent_to_vae(x, mean, std))
+    assert np.array_equal(ops.latent_normalize_t(T(x), T(mean), T(std)).cpu().numpy(),
+                          orc.latent_normalize(x, mean, std))
