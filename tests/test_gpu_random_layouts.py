@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import assert_close
+from conftest import assert_close, scaled_error
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-5
@@ -218,3 +218,51 @@ def test_latent_random_shapes(ops, orc, dev, seed):
     assert np.array_equal(ops.latent_to_vae_t(T(x), T(mean), T(std)).cpu().numpy(), orc.latent_to_vae(x, mean, std))
     assert np.array_equal(ops.latent_normalize_t(T(x), T(mean), T(std)).cpu().numpy(),
                           orc.latent_normalize(x, mean, std))
+
+
+@pytest.mark.parametrize("seed", range(16))
+def test_chain_random_topologies(ops, orc, dev, seed):
+    """Random decoder topologies (1-8 stages, widths, strides, 0-4 residual units, channel
+    counts), frame counts, F32- or F16-stored parameters and the tanh epilogue, through the
+    device decode and the stage capture, against the oracle's node-by-node chain.
+
+    With identity stand-ins for the residual convs, every residual unit feeds its SnakeBeta
+    output back into the stream and roughly doubles it, so deep random chains are badly
+    conditioned: the oracle's own output moves by up to ~2e-4 (scaled) when its input moves
+    by one ulp.  Each tensor's bar is therefore max(1e-5, 10 x that measured 1-ulp
+    sensitivity of the oracle); the BASELINE-shape chain tests keep a flat 1e-5.  A layout or
+    indexing error shows as an O(1) difference."""
+    rng = np.random.default_rng(9000 + seed)
+    t = ops.Topology()
+    t.latent_dim, t.audio_channels = int(rng.integers(1, 17)), int(rng.integers(1, 4))
+    t.entry_width, t.n_stages = int(rng.integers(1, 97)), int(rng.integers(1, 9))
+    total = 1
+    for s in range(t.n_stages):
+        t.stage_width[s] = int(rng.integers(1, 65))
+        t.stage_stride[s] = int(rng.integers(1, 7)) if total < 2000 else 1
+        total *= t.stage_stride[s]
+    t.n_residual = int(rng.integers(0, 5))
+    for r in range(t.n_residual):
+        t.dilation[r] = int(rng.choice([1, 3, 9, 27]))
+    frames = int(rng.integers(1, 41))
+    tanh = bool(rng.integers(0, 2))
+    params = (0.1 * rng.standard_normal(ops.param_count(t))).astype(np.float32)
+    if rng.integers(0, 2):
+        params = params.astype(np.float16)
+    latent = rng.standard_normal((t.latent_dim, frames)).astype(np.float32)
+    chain = ops.VaeChain(t, params, max_frames=frames, device=0)
+    run = lambda lat: orc.vae_chain(t.as_list(), params.astype(np.float32), lat, frames,  # noqa: E731
+                                    t.audio_channels, frames * t.upsampling(), tanh=tanh, stages=True)
+    want, want_stages = run(latent)
+    nudged, nudged_stages = run(np.nextafter(latent, np.float32(np.inf)))  # the problem's own conditioning
+    bar = lambda a, b: max(TOL, 10 * scaled_error(b, a))  # noqa: E731
+    stages = [torch.full(w.shape, np.nan, device=dev) for w in want_stages]
+    chain.set_stage_capture(stages)
+    audio = torch.full((t.audio_channels, chain.samples(frames)), np.nan, device=dev)
+    chain.decode(torch.from_numpy(latent).to(dev), audio, frames, flags=ops.CHAIN_TANH if tanh else 0)
+    torch.cuda.synchronize()
+    what = f"topology={t.as_list()} frames={frames} tanh={tanh} f16={params.dtype == np.float16}"
+    assert_close(audio.cpu().numpy(), want, bar(want, nudged), what)
+    for s, (got, w, wn) in enumerate(zip(stages, want_stages, nudged_stages)):
+        assert_close(got.cpu().numpy(), w, bar(w, wn), f"{what} stage {s}")
+    chain.close()
