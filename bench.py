@@ -307,16 +307,43 @@ def config_block(args, ops, topo):
 
 # --------------------------------------------------------------------------- kernel sub-benchmarks (configs 0-2)
 
+L2_BYTES = 126 * 1024 * 1024
+KERNEL_LAUNCHES = 64  # back-to-back launches per timed repetition
+
+
+def input_sets(set_bytes: int) -> int:
+    """Input sets to rotate through so that a set is out of L2 when it comes round again:
+    at least 3, and together at least 2.5x the L2 capacity."""
+    return max(3, -(-int(2.5 * L2_BYTES) // max(set_bytes, 1)))
+
+
 def kernel_suite(ops, dev, peak, steps, warmup):
+    """Configs 0-2 kernels.  `ms` is the per-launch time of KERNEL_LAUNCHES back-to-back launches
+    between one pair of CUDA events, rotating over input sets larger than L2 in total (median of
+    `steps` repetitions); `ms_single_launch` is one launch after an L2 flush, bracketed by its own
+    events, which also counts the launch latency and sits on the event timer's 2 us tick."""
     import torch
 
     rng = np.random.default_rng(SEED)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > L2
     stream = torch.cuda.current_stream(dev)
 
-    def timeit(fn):
-        for _ in range(warmup):
-            fn()
+    def timeit_rotating(fns):
+        for i in range(max(warmup, 1) * len(fns)):
+            fns[i % len(fns)]()
+        per_launch = []
+        for _ in range(steps):
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(KERNEL_LAUNCHES):
+                fns[i % len(fns)]()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            per_launch.append(e0.elapsed_time(e1) / KERNEL_LAUNCHES)
+        return statistics.median(per_launch)
+
+    def timeit_single(fn):
         times = []
         for _ in range(steps):
             # Cold, clean L2: writing 256 MB (> 126 MB L2) evicts every line; reading it
@@ -333,50 +360,69 @@ def kernel_suite(ops, dev, peak, steps, warmup):
 
     out = {}
 
-    def entry_(name, ms, nbytes, **kw):
+    def entry_(name, fns, nbytes, set_bytes, **kw):
+        ms = timeit_rotating(fns)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        out[name] = {"ms": ms, "GB/s": gbs, "frac": gbs / peak, "algorithmic_bytes": nbytes, **kw}
+        out[name] = {"ms": ms, "GB/s": gbs, "frac": gbs / peak, "algorithmic_bytes": nbytes,
+                     "input_sets": len(fns), "bytes_touched_per_set": set_bytes,
+                     "launches_per_timing": KERNEL_LAUNCHES, "ms_single_launch": timeit_single(fns[0]), **kw}
 
     # config 0: SnakeBeta F32 [128, 483840]
     x = torch.from_numpy(rng.standard_normal((128, 483840), dtype=np.float32)).to(dev)
     a = torch.from_numpy((0.1 * rng.standard_normal(128)).astype(np.float32)).to(dev)
     b = torch.from_numpy((0.1 * rng.standard_normal(128)).astype(np.float32)).to(dev)
-    y = torch.empty_like(x)
-    entry_("snakebeta_f32[128,483840]", timeit(lambda: ops.snakebeta_t(x, a, b, out=y)), 8 * x.numel())
-    del x, y
+    set_bytes = 8 * x.numel()
+    sets = [(x if i == 0 else x.clone(), torch.empty_like(x)) for i in range(input_sets(set_bytes))]
+    entry_("snakebeta_f32[128,483840]", [lambda s=s: ops.snakebeta_t(s[0], a, b, out=s[1]) for s in sets],
+           8 * x.numel(), set_bytes)
+    del x, sets
     # config 1: add + RMSNorm / LayerNorm F16 [4096, 1536]; weight norm F32 [1024, 7168]
     xh = torch.from_numpy(rng.standard_normal((4096, 1536)).astype(np.float16)).to(dev)
     rh = torch.from_numpy(rng.standard_normal((4096, 1536)).astype(np.float16)).to(dev)
     g = torch.from_numpy((1 + 0.02 * rng.standard_normal(1536)).astype(np.float32)).to(dev)
     be = torch.from_numpy((0.02 * rng.standard_normal(1536)).astype(np.float32)).to(dev)
-    h, yy = torch.empty_like(xh), torch.empty_like(xh)
-    entry_("add_rmsnorm_f16[4096,1536]", timeit(lambda: ops.add_rmsnorm_t(xh, rh, g, 1e-6, h_out=h, y_out=yy)),
-           8 * xh.numel())
+    set_bytes = 8 * xh.numel()
+    sets = [(xh.clone(), rh.clone(), torch.empty_like(xh), torch.empty_like(xh))
+            for _ in range(input_sets(set_bytes))]
+    entry_("add_rmsnorm_f16[4096,1536]",
+           [lambda s=s: ops.add_rmsnorm_t(s[0], s[1], g, 1e-6, h_out=s[2], y_out=s[3]) for s in sets],
+           8 * xh.numel(), set_bytes)
     entry_("add_layernorm_f16[4096,1536]",
-           timeit(lambda: ops.add_layernorm_t(xh, rh, g, be, 1e-5, h_out=h, y_out=yy)), 8 * xh.numel())
+           [lambda s=s: ops.add_layernorm_t(s[0], s[1], g, be, 1e-5, h_out=s[2], y_out=s[3]) for s in sets],
+           8 * xh.numel(), set_bytes)
+    del sets
     v = torch.from_numpy((0.02 * rng.standard_normal((1024, 7168))).astype(np.float32)).to(dev)
     gg = torch.from_numpy(rng.uniform(0.5, 1.5, 1024).astype(np.float32)).to(dev)
-    w = torch.empty_like(v)
-    entry_("weightnorm_f32[1024,7168]", timeit(lambda: ops.weightnorm_t(v, gg, w=w)), 8 * v.numel())
+    set_bytes = 8 * v.numel()
+    sets = [(v.clone(), torch.empty_like(v)) for _ in range(input_sets(set_bytes))]
+    entry_("weightnorm_f32[1024,7168]", [lambda s=s: ops.weightnorm_t(s[0], gg, w=s[1]) for s in sets],
+           8 * v.numel(), set_bytes)
+    del sets
     # config 2: 50-step CFG + Euler on [2, 64, 252]
     n, S = 2 * 64 * 252, 50
     st0 = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).to(dev)
     vu = torch.from_numpy(rng.standard_normal((S, n)).astype(np.float32)).to(dev)
     vc = torch.from_numpy(rng.standard_normal((S, n)).astype(np.float32)).to(dev)
-    st = st0.clone()
-    entry_("cfg_euler_f32[2,64,252]x50", timeit(
-        lambda: ops.cfg_euler_multi_t(st, None, None, vu, vc, batch=2, prefix=0, first_step=0, count=S, steps=S,
-                                      guidance=1.5)), 4 * n * (2 * S + 2), note="latency-bound: 13 MB")
-    # What a plain device copy of the same byte count reaches at these sizes (torch, not ours):
-    # the achievable ceiling for ~50 MB kernels, where launch and ramp-up are a large share.
+    set_bytes = 4 * n * (2 * S + 2)
+    sets = [(st0.clone(), vu.clone(), vc.clone()) for _ in range(input_sets(set_bytes))]
+    entry_("cfg_euler_f32[2,64,252]x50",
+           [lambda s=s: ops.cfg_euler_multi_t(s[0], None, None, s[1], s[2], batch=2, prefix=0, first_step=0,
+                                              count=S, steps=S, guidance=1.5) for s in sets],
+           4 * n * (2 * S + 2), set_bytes, note="latency-bound: 13 MB")
+    del sets
+    # What a plain device copy of the same byte count reaches at these sizes (torch, not ours), timed
+    # the same way: the achievable ceiling for ~50 MB kernels, where ramp-up and drain are a large share.
     for mb in (50, 496):
         src = torch.empty(mb * 1024 * 1024 // 8, dtype=torch.float32, device=dev)
-        dst = torch.empty_like(src)
-        ms = timeit(lambda: dst.copy_(src))
-        out[f"torch_copy_{mb}MB_reference"] = {"ms": ms, "GB/s": 2 * src.numel() * 4 / (ms * 1e-3) / 1e9,
-                                              "frac": 2 * src.numel() * 4 / (ms * 1e-3) / 1e9 / peak}
-    # The ~13-60 MB kernels against what a plain device copy of ~50 MB reaches (launch, ramp-up and one
-    # DRAM round trip dominate at that size): GB/s of the kernel / GB/s of that copy.
+        set_bytes = 2 * src.numel() * 4
+        sets = [(src.clone(), torch.empty_like(src)) for _ in range(input_sets(set_bytes))]
+        ms = timeit_rotating([lambda s=s: s[1].copy_(s[0]) for s in sets])
+        out[f"torch_copy_{mb}MB_reference"] = {"ms": ms, "GB/s": set_bytes / (ms * 1e-3) / 1e9,
+                                              "frac": set_bytes / (ms * 1e-3) / 1e9 / peak,
+                                              "input_sets": len(sets)}
+        del sets
+    # The ~13-60 MB kernels against what a plain device copy of ~50 MB reaches: GB/s of the kernel /
+    # GB/s of that copy.
     copy_gbs = out["torch_copy_50MB_reference"]["GB/s"]
     for name in ("add_rmsnorm_f16[4096,1536]", "add_layernorm_f16[4096,1536]", "weightnorm_f32[1024,7168]",
                  "cfg_euler_f32[2,64,252]x50"):

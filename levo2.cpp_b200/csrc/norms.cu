@@ -2,12 +2,18 @@
 //
 // Every form reads x and r from HBM once and writes h and y once: 8 B per
 // element for F16 activations.
-// Staged path (the common case: rows of <= 12.5 KB, 16-byte aligned): one warp
+// Register path (the common case: 16-byte aligned rows of at most 4 KB, i.e.
+// F16 dim <= 2048 / F32 dim <= 1024, without the Flow modulation): one warp per
+// row, 8 rows per CTA, x and r copied into shared memory with cp.async, then
+// held packed in registers while the statistics and y are computed; gamma and
+// beta staged once per CTA; about two rows per warp so the next row's copies
+// overlap the current row's arithmetic (4096 x 1536 F16: 296 CTAs).
+// Staged path (longer rows of <= 12.5 KB, and the Flow adaLN form): one warp
 // per row, 8 rows per CTA.  x and r are copied into shared memory with cp.async
-// so the whole input is in flight at once without holding it in registers
-// (4096 x 1536 F16: 48 KB per CTA, 4 CTAs per SM, one wave); h = x + r is
-// written back over x, the row statistics are reduced with warp shuffles
-// (LayerNorm two-pass over shared memory), and y leaves in 16-byte stores.
+// so the whole input is in flight at once without holding it in registers;
+// h = x + r is written back over x, the row statistics are reduced with warp
+// shuffles (LayerNorm two-pass over shared memory), and y leaves in 16-byte
+// stores.
 // Vector path (longer rows): a row group of 32*wpr threads keeps the row in
 // registers (<= 64 F32 values per thread) and reduces across warps in shared
 // memory.  Scalar path (rows whose byte length is not a multiple of 16, or
@@ -317,6 +323,9 @@ struct Chunk<__half> {
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
+    __device__ static float first(const uint4 &c) {
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(c.x & 0xffffu)));
+    }
     // x + r rounded to F16 in one HADD2 per pair.  The F32 sum of two F16
     // values rounded to F16 is the same number: F32 carries 24 >= 2*11 + 1
     // significand bits, so the double rounding is innocuous (S. A. Figueroa,
@@ -336,6 +345,7 @@ struct Chunk<__half> {
 template <>
 struct Chunk<float> {
     static constexpr int kN = 4;
+    __device__ static float first(const uint4 &c) { return __uint_as_float(c.x); }
     __device__ static void unpack(const uint4 &c, float *v) {
         v[0] = __uint_as_float(c.x);
         v[1] = __uint_as_float(c.y);
@@ -500,6 +510,252 @@ __global__ void __launch_bounds__(kStagedRows * 32) add_norm_staged_kernel(const
     }
 }
 
+// Register form (rows of at most 32 * kRegsMaxCpl 16-byte chunks; add+norm
+// without the Flow modulation).  Like the staged form, a warp's row is copied
+// into shared memory with cp.async, one warp per row.  Once it lands the row
+// is read out of shared memory in one unrolled burst and held packed in the
+// activation type (h = x + r, CPL 16-byte chunks per lane), so the reductions
+// and the output pass are straight-line code on registers.  gamma (and beta)
+// are copied into shared memory once per CTA, ahead of the rows, so the output
+// pass never waits on L2.  A warp with a further row issues that row's copies
+// as soon as the current row is in registers, overlapping them with its
+// arithmetic.
+//
+// Rows of one wave land at nearly the same time, so the SM's issue slots, not
+// the memory system, set the tail of a launch: the per-row instruction count is
+// kept low by making the F16-boundary rounding a template parameter and by
+// branching on the residual / h_out pointers once per row, not per chunk, and
+// LayerNorm takes its mean and variance in one pass over the registers
+// (shifted sums, below) instead of two.  RMSNorm keeps the rounded steps of
+// norm_row_from_smem (same per-lane order of the paired partial sums, same
+// butterfly): both forms give the same bits.  For LayerNorm the two forms
+// differ only in the rounding of the statistics (a few F32 ulp).
+constexpr int kRegsMaxCpl = 8;
+constexpr int kRegsWarps = 8;        // warps (= rows in flight) per CTA
+constexpr int kRegsRowsPerWarp = 2;  // rows per warp a launch aims for (copies of the next row overlap)
+
+template <typename T, bool LAYER, bool BOUND>
+__device__ __forceinline__ uint4 norm_chunk_out(uint4 hc, const float4 *gs, const float4 *bs, int i, float mean,
+                                                float scale) {
+    constexpr int N = Chunk<T>::kN;
+    float h[N];
+    Chunk<T>::unpack(hc, h);
+#pragma unroll
+    for (int q = 0; q < N / 4; ++q) {
+        const float4 g = gs[i * (N / 4) + q];
+        float2 v0 = make_float2(h[4 * q], h[4 * q + 1]);
+        float2 v1 = make_float2(h[4 * q + 2], h[4 * q + 3]);
+        if (LAYER) {
+            v0 = __fadd2_rn(v0, pair(-mean));
+            v1 = __fadd2_rn(v1, pair(-mean));
+        }
+        v0 = __fmul2_rn(v0, pair(scale));
+        v1 = __fmul2_rn(v1, pair(scale));
+        if (BOUND) {
+            v0 = make_float2(Act<T>::round(v0.x), Act<T>::round(v0.y));
+            v1 = make_float2(Act<T>::round(v1.x), Act<T>::round(v1.y));
+        }
+        v0 = __fmul2_rn(v0, make_float2(g.x, g.y));
+        v1 = __fmul2_rn(v1, make_float2(g.z, g.w));
+        if (LAYER) {
+            const float4 b = bs[i * (N / 4) + q];
+            v0 = __fadd2_rn(v0, make_float2(b.x, b.y));
+            v1 = __fadd2_rn(v1, make_float2(b.z, b.w));
+        }
+        h[4 * q] = v0.x;
+        h[4 * q + 1] = v0.y;
+        h[4 * q + 2] = v1.x;
+        h[4 * q + 3] = v1.y;
+    }
+    return Chunk<T>::pack(h);
+}
+
+// Paired partial sum of one chunk (sum of values for LayerNorm, of squares for RMSNorm).
+template <typename T, bool LAYER>
+__device__ __forceinline__ float chunk_sum(uint4 hc) {
+    constexpr int N = Chunk<T>::kN;
+    float h[N];
+    Chunk<T>::unpack(hc, h);
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < N; j += 2) {
+        const float2 v = make_float2(h[j], h[j + 1]);
+        acc = LAYER ? __fadd2_rn(acc, v) : __ffma2_rn(v, v, acc);
+    }
+    return acc.x + acc.y;
+}
+
+template <typename T, bool LAYER, bool BOUND, int CPL>
+__global__ void __launch_bounds__(kRegsWarps * 32, 4) add_norm_regs_kernel(const NormArgs a) {
+    extern __shared__ uint4 sbuf[];
+    constexpr int N = Chunk<T>::kN;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int chunks = a.dim / N;   // 16-byte chunks of a row
+    const int pchunks = a.dim / 4;  // 16-byte chunks of gamma / beta
+    float4 *gs = reinterpret_cast<float4 *>(sbuf);
+    float4 *bs = gs + pchunks;
+    uint4 *xs = reinterpret_cast<uint4 *>(gs + (LAYER ? 2 : 1) * pchunks) + static_cast<size_t>(warp) * 2 * chunks;
+    uint4 *rs = xs + chunks;
+    const bool has_r = a.r != nullptr;
+    const bool has_h = has_r && a.h_out != nullptr;
+    const float inv_dim = 1.0f / static_cast<float>(a.dim);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * warps;
+    const size_t row_bytes = static_cast<size_t>(a.dim) * sizeof(T);
+    // number of this lane's chunks inside the row (chunks lane, lane + 32, ...)
+    const int mine = chunks > lane ? (chunks - lane + 31) / 32 : 0;
+
+    auto issue_row = [&](int64_t row) {
+        const char *xg = static_cast<const char *>(a.x) + row * row_bytes;
+        const char *rg = static_cast<const char *>(a.r) + row * row_bytes;
+#pragma unroll
+        for (int k = 0; k < CPL; ++k)
+            if (k < mine) cp_async16(xs + lane + 32 * k, xg + 16 * (lane + 32 * k));
+        if (has_r) {
+#pragma unroll
+            for (int k = 0; k < CPL; ++k)
+                if (k < mine) cp_async16(rs + lane + 32 * k, rg + 16 * (lane + 32 * k));
+        }
+    };
+
+    // group 0: the CTA's gamma / beta; group 1: this warp's first row
+    for (int i = threadIdx.x; i < pchunks; i += blockDim.x) {
+        cp_async16(gs + i, a.gamma + 4 * i);
+        if (LAYER) cp_async16(bs + i, a.beta + 4 * i);
+    }
+    cp_async_commit();
+    int64_t row = static_cast<int64_t>(blockIdx.x) * warps + warp;
+    if (row < a.rows) issue_row(row);
+    cp_async_commit();
+    cp_async_wait_group<1>();
+    __syncthreads();  // every thread's share of gamma / beta has landed
+
+    for (; row < a.rows; row += stride) {
+        cp_async_wait_group<0>();
+        __syncwarp();
+        // h = x + r (rounded to T), held packed; paired partial sums per chunk
+        uint4 hreg[CPL];
+        float sum = 0.f;
+        if (has_r) {
+#pragma unroll
+            for (int k = 0; k < CPL; ++k)
+                if (k < mine) hreg[k] = Chunk<T>::add(xs[lane + 32 * k], rs[lane + 32 * k]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < CPL; ++k)
+                if (k < mine) hreg[k] = xs[lane + 32 * k];
+        }
+        // the row is in registers: the next row's copies go out now, and h
+        // leaves before the reductions so its stores drain under their latency
+        __syncwarp();
+        const int64_t next = row + stride;
+        if (next < a.rows) issue_row(next);
+        cp_async_commit();
+        if (has_h) {
+            uint4 *hg = reinterpret_cast<uint4 *>(static_cast<char *>(a.h_out) + row * row_bytes);
+#pragma unroll
+            for (int k = 0; k < CPL; ++k)
+                if (k < mine) hg[lane + 32 * k] = hreg[k];
+        }
+
+        float mean = 0.f, scale;
+        if (LAYER) {
+            // One pass over the registers: sums of d = h - K and of d^2 around
+            // the row's first value K (shifted data: no cancellation between
+            // E[d^2] and E[d]^2 when |mean| >> stddev), then
+            // mean = K + E[d], var = E[d^2] - E[d]^2.
+            const float K = __shfl_sync(0xffffffffu, Chunk<T>::first(hreg[0]), 0);
+            float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) {
+                if (k < mine) {
+                    float h[N];
+                    Chunk<T>::unpack(hreg[k], h);
+#pragma unroll
+                    for (int j = 0; j < N; j += 2) {
+                        const float2 d = __fadd2_rn(make_float2(h[j], h[j + 1]), pair(-K));
+                        s1 = __fadd2_rn(s1, d);
+                        s2 = __ffma2_rn(d, d, s2);
+                    }
+                }
+            }
+            float sd = s1.x + s1.y, sq = s2.x + s2.y;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                sd += __shfl_xor_sync(0xffffffffu, sd, o);
+                sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            }
+            const float md = sd * inv_dim;
+            const float var = fmaxf(__fsub_rn(sq * inv_dim, md * md), 0.f);
+            mean = __fadd_rn(K, md);
+            scale = 1.0f / sqrtf(var + a.eps);
+        } else {
+#pragma unroll
+            for (int k = 0; k < CPL; ++k)
+                if (k < mine) sum += chunk_sum<T, LAYER>(hreg[k]);
+            sum = warp_sum(sum);
+            scale = 1.0f / sqrtf(sum * inv_dim + a.eps);
+        }
+        uint4 *yg = reinterpret_cast<uint4 *>(static_cast<char *>(a.y_out) + row * row_bytes);
+#pragma unroll
+        for (int k = 0; k < CPL; ++k)
+            if (k < mine)
+                yg[lane + 32 * k] = norm_chunk_out<T, LAYER, BOUND>(hreg[k], gs, bs, lane + 32 * k, mean, scale);
+    }
+    cp_async_wait_group<0>();  // nothing of this thread's is left in flight at exit
+}
+
+// Launches the register form when the row fits it; returns false (nothing
+// launched) otherwise.  CTAs of kRegsWarps warps; grid: a whole number of CTAs
+// per SM, enough for about kRegsRowsPerWarp rows per warp, at most the
+// resident capacity.  (Measured at [4096, 1536] F16: 8-warp CTAs with about
+// two rows per warp beat one wave of 8- or 16-warp CTAs and three rows per
+// warp, for both norms.)
+template <typename T, bool LAYER, bool BOUND, int CPL>
+bool launch_regs_cpl(const NormArgs &a, cudaStream_t stream) {
+    auto kernel = add_norm_regs_kernel<T, LAYER, BOUND, CPL>;
+    const size_t param_bytes = static_cast<size_t>(LAYER ? 2 : 1) * a.dim * sizeof(float);
+    const size_t smem = param_bytes + static_cast<size_t>(kRegsWarps) * 2 * a.dim * sizeof(T);
+    if (smem > kStagedMaxSmem) return false;
+    int resident = 0;
+    if (resident_ctas(reinterpret_cast<const void *>(kernel), kRegsWarps * 32, smem, &resident) != cudaSuccess) {
+        cudaGetLastError();  // clear the failed opt-in; the caller falls back
+        return false;
+    }
+    if (resident <= 0) return false;
+    const int64_t sms = sm_count();
+    const int64_t ctas_needed = (a.rows + kRegsWarps - 1) / kRegsWarps;
+    int64_t per_sm = (a.rows + sms * kRegsWarps * kRegsRowsPerWarp - 1) / (sms * kRegsWarps * kRegsRowsPerWarp);
+    per_sm = std::min<int64_t>(std::max<int64_t>(per_sm, 1), resident);
+    const int64_t grid = std::min<int64_t>(ctas_needed, sms * per_sm);
+    kernel<<<static_cast<unsigned>(grid), kRegsWarps * 32, smem, stream>>>(a);
+    return true;
+}
+
+template <typename T, bool LAYER, bool BOUND>
+bool launch_regs_b(const NormArgs &a, int cpl, cudaStream_t stream) {
+    switch (cpl) {
+        case 1: return launch_regs_cpl<T, LAYER, BOUND, 1>(a, stream);
+        case 2: return launch_regs_cpl<T, LAYER, BOUND, 2>(a, stream);
+        case 3: return launch_regs_cpl<T, LAYER, BOUND, 3>(a, stream);
+        case 4: return launch_regs_cpl<T, LAYER, BOUND, 4>(a, stream);
+        case 5:
+        case 6: return launch_regs_cpl<T, LAYER, BOUND, 6>(a, stream);
+        case 7:
+        case 8: return launch_regs_cpl<T, LAYER, BOUND, 8>(a, stream);
+        default: return false;
+    }
+}
+
+template <typename T, bool LAYER>
+bool launch_regs(const NormArgs &a, int cpl, cudaStream_t stream) {
+    if constexpr (sizeof(T) == 2) {
+        if (a.f16_boundary) return launch_regs_b<T, LAYER, true>(a, cpl, stream);
+    }
+    return launch_regs_b<T, LAYER, false>(a, cpl, stream);
+}
+
 // Fallback: one CTA per row, any dim and alignment.
 template <typename T, bool LAYER>
 __global__ void __launch_bounds__(kThreads) add_norm_scalar_kernel(const NormArgs a) {
@@ -604,6 +860,11 @@ int run_norm(const char *what, const void *x, const void *r, const float *gamma,
             if (ptrs[i] && !aligned_to(ptrs[i], 16)) staged = false;
         for (const void *m : mods)
             if (m && !aligned_to(m, 16)) staged = false;
+        if constexpr (!MOD) {
+            const int64_t chunks = dim * static_cast<int64_t>(sizeof(T)) / 16;
+            const int cpl = static_cast<int>((chunks + 31) / 32);
+            if (staged && cpl <= kRegsMaxCpl && launch_regs<T, LAYER>(a, cpl, stream)) return check_launch(what);
+        }
         if (staged) {
             auto kernel = add_norm_staged_kernel<T, LAYER, MOD>;
             int per_sm = 0;
