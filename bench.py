@@ -14,14 +14,16 @@ Extra keys of the JSON line:
   roofline     the dominant kernel class (CUDA events around each launch in the timed
                region) against the measured HBM copy bandwidth
   kernels      SnakeBeta (config 0), add+RMSNorm / add+LayerNorm / weight norm
-               (config 1) and the fused 50-step CFG+Euler (config 2) in GB/s, L2 flushed
-               between iterations (rank 0, N = 1 only)
-  cpu_baseline the CPU oracle (node-by-node restatement, all host threads) on one window of
-               a bounded frame count (rank 0, N = 1 only)
+               (config 1) and the fused 50-step CFG+Euler (config 2) in GB/s: per-launch
+               time of back-to-back launches over input sets larger than L2 in total
+               (rank 0, N = 1 only)
+  cpu_baseline the CPU oracle (node-by-node restatement, all host threads) on one whole
+               window of the same frame count (rank 0, N = 1 only)
 
 `--impl reference` times the reference's CPU path instead: the reference's GGML CPU
 backend cannot be built here (the ggml submodule is absent), so its node-by-node
-restatement (oracle/) runs on all host threads on a bounded sample per step.
+restatement (oracle/) runs on all host threads, one whole window per step.  That arm
+imports and loads nothing of levo2.cpp_b200.
 """
 from __future__ import annotations
 
@@ -43,7 +45,7 @@ sys.path.insert(0, str(ROOT))
 import __graft_entry__ as entry  # noqa: E402
 
 SEED = 1234
-FRAME_RATE = 25.0  # latent frames per audio second (src/levo-renderer-pattern.h:221)
+FRAME_RATE = 25.0  # latent frames per audio second (src/levo-renderer-pattern.h:16)
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "vae_decode_audio_sec_per_sec"
 _JSON_OUT = sys.stdout
@@ -97,8 +99,24 @@ def measured_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def make_params(ops, topo, seed=SEED) -> np.ndarray:
-    """Packed decoder parameters: SnakeBeta log-params ~ N(0, 0.1), biases ~ N(0, 0.02)."""
+def topology_list(topo) -> list[int]:
+    """Flat decoder topology: latent_dim, audio_channels, entry_width, S, widths[S], strides[S], R."""
+    return [int(v) for v in (topo.as_list() if hasattr(topo, "as_list") else topo)]
+
+
+def upsampling(topo_list) -> int:
+    s = topo_list[3]
+    out = 1
+    for v in topo_list[4 + s:4 + 2 * s]:
+        out *= v
+    return out
+
+
+def make_params(topo_list, seed=SEED) -> np.ndarray:
+    """Packed decoder parameters in the reference's tensor-inventory order (input bias; per stage
+    the upsample snake, upsample bias, per residual unit pre snake, conv.0 bias, post snake,
+    conv.1 bias; output snake): SnakeBeta log-params ~ N(0, 0.1), biases ~ N(0, 0.02).  Both arms
+    build the identical array from the flat topology."""
     rng = np.random.default_rng(seed)
     parts = []
 
@@ -109,22 +127,21 @@ def make_params(ops, topo, seed=SEED) -> np.ndarray:
     def bias(c):
         parts.append((0.02 * rng.standard_normal(c)).astype(np.float32))
 
-    bias(topo.entry_width)
-    cin = topo.entry_width
-    for s in range(topo.n_stages):
-        c = topo.stage_width[s]
+    entry_width, n_stages = topo_list[2], topo_list[3]
+    widths, n_residual = topo_list[4:4 + n_stages], topo_list[4 + 2 * n_stages]
+    bias(entry_width)
+    cin = entry_width
+    for c in widths:
         snake(cin)
         bias(c)
-        for _ in range(topo.n_residual):
+        for _ in range(n_residual):
             snake(c)
             bias(c)
             snake(c)
             bias(c)
         cin = c
     snake(cin)
-    p = np.concatenate(parts)
-    assert p.size == ops.param_count(topo)
-    return p
+    return np.concatenate(parts)
 
 
 def make_latents(windows, latent_dim, frames, seed=SEED) -> np.ndarray:
@@ -237,50 +254,48 @@ class Dist:
 
 # --------------------------------------------------------------------------- CPU arms
 
-def cpu_chain_sample(orc, ops, topo, params, target_s: float, max_frames: int):
-    """Times the oracle chain on one window; frames sized for ~target_s of CPU work."""
+def cpu_window_decoder(orc, topo_list, params, frames: int):
+    """The oracle chain on one whole window of `frames` latent frames, on all host threads; returns
+    (cores, run) where run(latent) decodes one window and returns its seconds."""
     cores = host_cores()
-    rng = np.random.default_rng(SEED + 7)
-    probe = 2
-    lat = rng.standard_normal((topo.latent_dim, probe), dtype=np.float32)
-    t0 = time.perf_counter()
-    orc.vae_chain(topo.as_list(), params, lat, probe, topo.audio_channels, probe * topo.upsampling(), tanh=True,
-                  threads=cores)
-    per_frame = max((time.perf_counter() - t0) / probe, 1e-4)
-    frames = int(max(2, min(max_frames, target_s / per_frame)))
-    lat = rng.standard_normal((topo.latent_dim, frames), dtype=np.float32)
+    samples = frames * upsampling(topo_list)
 
-    def run():
+    def run(latent):
         t = time.perf_counter()
-        orc.vae_chain(topo.as_list(), params, lat, frames, topo.audio_channels, frames * topo.upsampling(),
-                      tanh=True, threads=cores)
+        orc.vae_chain(topo_list, params, latent, frames, topo_list[1], samples, tanh=True, threads=cores)
         return time.perf_counter() - t
 
-    return frames, cores, run
+    return cores, run
 
 
 def reference_arm(args):
+    """The reference's CPU path for this workload: its node-by-node restatement (oracle/), one whole
+    window of args.frames latent frames per step, rotating through the same seeded latents as the
+    own arm.  Nothing of levo2.cpp_b200 is imported or loaded here: the topology and the parameter
+    packing are the oracle side's own (oracle.REFERENCE_TOPOLOGY / param_count)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    pkg = entry.load_package()
-    ops = pkg.ops
     orc = entry.load_oracle()
-    topo = ops.reference_topology()
-    params = make_params(ops, topo)
-    frames, cores, run = cpu_chain_sample(orc, ops, topo, params, target_s=1.5, max_frames=args.frames)
-    for _ in range(args.warmup):
-        run()
-    secs = [run() for _ in range(args.steps)]
+    topo = list(orc.REFERENCE_TOPOLOGY)
+    params = make_params(topo)
+    if params.size != orc.param_count(topo):
+        raise SystemExit("reference arm: parameter packing does not match the reference inventory")
+    latents = make_latents(args.windows, topo[0], args.frames)
+    cores, run = cpu_window_decoder(orc, topo, params, args.frames)
+    for i in range(args.warmup):
+        run(latents[i % args.windows])
+    secs = [run(latents[i % args.windows]) for i in range(args.steps)]
     mean = sum(secs) / len(secs)
-    value = frames / FRAME_RATE / mean
-    sample = (f"one window of {frames} latent frames ({frames / FRAME_RATE:.2f} s of audio) per step, reference "
-              f"topology, tanh epilogue, conv stand-ins; {cores} threads on {cpu_model()}")
+    value = args.frames / FRAME_RATE / mean
+    sample = (f"one whole window of {args.frames} latent frames ({args.frames / FRAME_RATE:g} s of audio) per step, "
+              f"rotating through the {args.windows} seeded latents; reference topology, tanh epilogue, conv "
+              f"stand-ins; {cores} threads on {cpu_model()}")
     line = {
         "metric": METRIC, "value": value, "unit": "audio-s/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": f"synthetic (seed {SEED})", "impl": "reference",
-        "config": config_block(args, ops, topo),
+        "config": config_block(args, topo),
         "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": ("the reference's GGML CPU backend is not buildable here (ggml submodule absent); this is its "
@@ -290,14 +305,14 @@ def reference_arm(args):
     return 0
 
 
-def config_block(args, ops, topo):
+def config_block(args, topo_list):
     return {
         "workload": (f"BASELINE config 4: {args.windows} independent {args.frames / FRAME_RATE:g} s stereo windows "
                      f"(latent [64,{args.frames}]) through the Oobleck decoder elementwise chain, reference "
                      "topology 2048->1024->512->256->128->128, strides 10,6,4,4,2, 3 residual units/stage, "
                      f"{'tanh epilogue, ' if not args.no_tanh else ''}convs = built-in stand-ins"),
         "windows": args.windows, "frames": args.frames,
-        "samples_per_window": args.frames * topo.upsampling(),
+        "samples_per_window": args.frames * upsampling(topo_list),
         "parallelism": f"windows sharded over {args.gpus} GPU(s), no data collective, host gather",
         "l2": "inputs larger than L2 (each step streams ~28 GB per window)",
         "timing": "value: K steps between barriers, CUDA events at the ends only; roofline and per-class split: "
@@ -441,7 +456,10 @@ def own_arm(args):
     pkg = entry.load_package()
     ops, sharding = pkg.ops, pkg.sharding
     topo = ops.reference_topology()
-    params = make_params(ops, topo)
+    topo_l = topology_list(topo)
+    params = make_params(topo_l)
+    if params.size != ops.param_count(topo):
+        raise SystemExit("parameter packing does not match levo_vae_param_count")
     latents = make_latents(args.windows, topo.latent_dim, args.frames)
     start, stop = sharding.shard_range(args.windows, d.rank, d.world)
     mine = stop - start
@@ -531,7 +549,10 @@ def own_arm(args):
         if tfile.exists():
             tb = json.loads(tfile.read_text()).get(dom_name)
             if tb and dom["launches"]:
-                traffic = tb["dram_bytes_per_elem"] * dom["elements"] / dom["launches"]
+                # DRAM bytes per algorithmic byte of one ncu-captured launch of this class, applied to
+                # the class's mean algorithmic bytes per launch (the class mixes 16 B/elem units with
+                # the 12 B/elem last unit of each stage)
+                traffic = tb["dram_bytes_per_elem"] / tb["algorithmic_bytes_per_elem"] * dom["bytes"] / dom["launches"]
         elementwise_ms = sum(v["ms"] for v in work.values()) / args.steps
         line = {
             "metric": METRIC, "value": value, "unit": "audio-s/s", "n_gpus": d.world, "steps": args.steps,
@@ -539,7 +560,7 @@ def own_arm(args):
             "vs_baseline": None, "dtype": "f32",
             "data": f"synthetic (seed {SEED}; BASELINE config 4 shapes: latents ~N(0,1), log-params ~N(0,0.1), "
                     "biases ~N(0,0.02))",
-            "config": config_block(args, ops, topo),
+            "config": config_block(args, topo_l),
             "e2e": {"value": audio_seconds / (e2e_ms * 1e-3), "unit": "audio-s/s",
                     "h2d_bytes_per_step": int(latents.nbytes),
                     "d2h_bytes_per_step": int(args.windows * topo.audio_channels * samples * 4),
@@ -561,12 +582,12 @@ def own_arm(args):
             line["kernels"] = kernel_suite(ops, dev, peak, steps=max(args.steps, 5), warmup=args.warmup)
         if d.world == 1 and not args.no_cpu:
             orc = entry.load_oracle()
-            frames, cores, run = cpu_chain_sample(orc, ops, topo, params, target_s=10.0, max_frames=args.frames)
-            secs = run()
+            cores, run = cpu_window_decoder(orc, topo_l, params, args.frames)
+            secs = run(latents[0])
             line["cpu_baseline"] = {
-                "value": frames / FRAME_RATE / secs, "unit": "audio-s/s", "cores": cores, "kind": "port",
-                "sample": f"one window of {frames} latent frames ({frames / FRAME_RATE:.2f} s audio), same chain, "
-                          f"{secs:.1f} s on {cores} threads of {cpu_model()}"}
+                "value": args.frames / FRAME_RATE / secs, "unit": "audio-s/s", "cores": cores, "kind": "port",
+                "sample": f"one whole window of {args.frames} latent frames ({args.frames / FRAME_RATE:g} s audio), "
+                          f"the same chain, {secs:.1f} s on {cores} threads of {cpu_model()}"}
     chain.close()
     d.close()
     if line is not None:

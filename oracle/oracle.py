@@ -42,7 +42,8 @@ _SIGS = {
     "oracle_greedy_tokens_f32": [_P, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P],
     "oracle_latent_to_vae_f32": [_P, _P, _P, _I64, _I64, _P],
     "oracle_latent_normalize_f32": [_P, _P, _P, _I64, _I64, _P],
-    "oracle_cfg_euler_f32": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _F, _F],
+    "oracle_cfg_euler_f32": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _F, _F,
+                             ctypes.POINTER(_I64)],
 }
 
 _REF_SIGS = {
@@ -60,6 +61,45 @@ _REF_SIGS = {
 
 _lib = None
 _ref = None
+
+# --------------------------------------------------------------------------- reference decoder topology
+# The reference's Oobleck decoder, restated on the test side (independent of liblevo_b200):
+#   input conv latent_dim -> 2048 with bias        src/levo-vae-model.cpp:172
+#   stage output widths 1024, 512, 256, 128, 128   src/levo-vae-model.cpp:174
+#   strides 10, 6, 4, 4, 2                         src/levo-vae-model.cpp:175, src/levo-vae.cpp:215
+#   3 residual units per stage, dilations 1, 3, 9  src/levo-vae-model.cpp:181, src/levo-vae.cpp:216
+#   output snake on 128 channels, conv to 2 audio channels without bias   src/levo-vae-model.cpp:190-191
+# latent_dim 64 and 2 audio channels are the VAE hyper-parameters the reference validates.
+# Flat form, as vae_chain takes it: latent_dim, audio_channels, entry_width, S, widths[S], strides[S], R.
+REFERENCE_TOPOLOGY = (64, 2, 2048, 5, 1024, 512, 256, 128, 128, 10, 6, 4, 4, 2, 3)
+REFERENCE_DILATIONS = (1, 3, 9)
+
+
+def topology_fields(topology) -> dict:
+    t = [int(v) for v in topology]
+    s = t[3]
+    return {"latent_dim": t[0], "audio_channels": t[1], "entry_width": t[2], "n_stages": s,
+            "widths": t[4:4 + s], "strides": t[4 + s:4 + 2 * s], "n_residual": t[4 + 2 * s]}
+
+
+def param_count(topology) -> int:
+    """Elementwise parameters of the decoder in the reference's tensor-inventory order
+    (src/levo-vae-model.cpp:172-191): input bias; per stage the upsample snake (2 x Cin),
+    upsample bias, and per residual unit pre snake, conv.0 bias, post snake, conv.1 bias;
+    the output snake."""
+    f = topology_fields(topology)
+    n, cin = f["entry_width"], f["entry_width"]
+    for c in f["widths"]:
+        n += 2 * cin + c + 6 * c * f["n_residual"]
+        cin = c
+    return n + 2 * cin
+
+
+def upsampling(topology) -> int:
+    out = 1
+    for s in topology_fields(topology)["strides"]:
+        out *= s
+    return out
 
 
 def lib() -> ctypes.CDLL:
@@ -239,19 +279,30 @@ def cfg_combine(u, c, g) -> np.ndarray:
     return out
 
 
-def cfg_euler(state, noise, context, uncond, cond, *, batch, prefix, first_step, count, steps, cfg=True,
-              guidance=1.5, sigma_min=1e-4):
-    """Returns (state_after, ok)."""
+def cfg_euler_checked(state, noise, context, uncond, cond, *, batch, prefix, first_step, count, steps, cfg=True,
+                      guidance=1.5, sigma_min=1e-4):
+    """Returns (state_after, failure, failed_step): failure is None, "velocity" or "state"; on a
+    failure state_after is the checkpoint of the steps completed before failed_step."""
     st = _f32(state).copy()
     n = st.size
     nz = _f32(noise) if noise is not None else np.zeros(n, np.float32)
     cx = _f32(context) if context is not None else np.zeros(n, np.float32)
     u = _f32(uncond) if uncond is not None else np.zeros(1, np.float32)
     c = _f32(cond) if (cond is not None and cfg) else None
+    failed = _I64(-1)
     rc = lib().oracle_cfg_euler_f32(_p(st), _p(nz), _p(cx), _p(u), _p(c), batch, n // batch, prefix, first_step,
-                                    count, steps, 1 if cfg else 0, guidance, sigma_min)
-    assert rc in (0, -1)
-    return st, rc == 0
+                                    count, steps, 1 if cfg else 0, guidance, sigma_min, ctypes.byref(failed))
+    assert rc in (0, -1, -3)
+    return st, {0: None, -1: "velocity", -3: "state"}[rc], failed.value
+
+
+def cfg_euler(state, noise, context, uncond, cond, *, batch, prefix, first_step, count, steps, cfg=True,
+              guidance=1.5, sigma_min=1e-4):
+    """Returns (state_after, ok)."""
+    st, failure, _ = cfg_euler_checked(state, noise, context, uncond, cond, batch=batch, prefix=prefix,
+                                       first_step=first_step, count=count, steps=steps, cfg=cfg,
+                                       guidance=guidance, sigma_min=sigma_min)
+    return st, failure is None
 
 
 def assemble_windows(windows, hop, overlap, target) -> np.ndarray:
@@ -310,7 +361,8 @@ def ref_combine_renderer_cfg(u, c, g) -> np.ndarray:
 def ref_solve_flow_euler(noise, context, frames, latent_dim, incontext_frames, sigma_min, steps, uncond, cond,
                          cfg=True, guidance=1.5, resume_step=-1, resume_state=None, pause_after=-1,
                          want_seen=False):
-    """Returns (status, state, completed_steps, seen) — status 0 solved, 1 paused."""
+    """Returns (status, state, completed_steps, seen) — status 0 solved, 1 paused, 2 stopped by a
+    non-finite velocity or state (state = the reference's checkpoint, message in ref_last_message())."""
     n = frames * latent_dim
     noise, context, uncond = _f32(noise), _f32(context), _f32(uncond)
     cond = _f32(cond) if cond is not None else uncond
@@ -321,9 +373,15 @@ def ref_solve_flow_euler(noise, context, frames, latent_dim, incontext_frames, s
     rc = ref().ref_solve_flow_euler(_p(noise), _p(context), frames, latent_dim, incontext_frames, sigma_min, steps,
                                     _p(uncond), _p(cond), 1 if cfg else 0, guidance, resume_step, _p(rs),
                                     pause_after, _p(seen), _p(out), ctypes.byref(done))
+    if rc == -2:
+        return 2, out, done.value, seen
     if rc < 0:
         raise ValueError(_ref_err())
     return rc, out, done.value, seen
+
+
+def ref_last_message() -> str:
+    return _ref_err()
 
 
 def ref_make_renderer_schedule(source_frames: int, max_windows: int = 4096):

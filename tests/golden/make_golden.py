@@ -1,8 +1,8 @@
 """Generates the golden fixtures in tests/golden/ from the reference itself.
 
 Run where the reference tree exists (its path in LEVO_REFERENCE_ROOT, or the
-default checkout location the oracle Makefile also uses) after `make -C oracle`
-has built oracle/_ref/libref_levo.so:
+reference_path of BASELINE.json) after `make -C oracle REF_ROOT=...` has built
+oracle/_ref/libref_levo.so:
 
     python tests/golden/make_golden.py
 
@@ -29,7 +29,12 @@ import numpy as np
 
 HERE = pathlib.Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = pathlib.Path(os.environ.get("LEVO_REFERENCE_ROOT", "/root/reference"))
+sys.path.insert(0, str(ROOT))
+import __graft_entry__ as _entry  # noqa: E402
+
+REF = _entry.reference_root()
+if REF is None:
+    raise SystemExit("make_golden: the reference tree was not found (set LEVO_REFERENCE_ROOT)")
 
 
 def _libm():
