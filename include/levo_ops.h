@@ -73,7 +73,7 @@ LEVO_OPS_API const char *levo_ops_last_error(void);
  * arithmetic the kernels apply to log parameters, so a SnakeBeta launch given
  * the outputs with LEVO_DTYPE_SNAKE_PREPARED is bit-identical to one given the
  * logs.  The reference recomputes exp(alpha_log) and exp(beta_log) + 1e-9 as
- * graph nodes on every call (src/levo-audio-ops.cpp:181-185); it has no
+ * graph nodes on every call (src/levo-audio-ops.cpp:146-151); it has no
  * separate entry point.  alpha_log / beta_log are F32 or F16 (`param_dtype`).
  * Zero channels is a no-op.
  */
@@ -85,9 +85,9 @@ LEVO_OPS_API int levo_snake_params_prepare(const void *alpha_log, const void *be
  * y[c][t] = x[c][t] + sin(x[c][t]*alpha_c)^2 / beta_c
  *   alpha_c = exp(alpha_log[c]),  beta_c = exp(beta_log[c]) + 1e-9
  * Replaces levo::detail::snake_beta (src/levo-audio-ops.h:30-33,
- * src/levo-audio-ops.cpp:160-187) as used by run_snake (src/levo-vae.cpp:80-88).
+ * src/levo-audio-ops.cpp:125-152) as used by run_snake (src/levo-vae.cpp:80-88).
  * alpha_log / beta_log are [channels] in F32 or F16 (`param_dtype`), promoted to
- * F32 in-kernel as the reference's ggml_cast does (src/levo-audio-ops.cpp:67-72),
+ * F32 in-kernel as the reference's ggml_cast does (src/levo-audio-ops.cpp:32-37),
  * or LEVO_DTYPE_SNAKE_PREPARED outputs of levo_snake_params_prepare().
  * ldx / ldy are row strides in elements (>= time).  Dense rows use the 256-bit
  * vector path; strided rows use the scalar path.
@@ -102,7 +102,7 @@ LEVO_OPS_API int levo_snakebeta_f32(const float *x, int64_t ldx,
 /* ------------------------------------------------------------------------- */
 /*
  * out[c][t] = in[c][t] + bias[c]; bias F32 or F16.
- * Replaces add_channel_bias (src/levo-audio-ops.cpp:74-87).
+ * Replaces add_channel_bias (src/levo-audio-ops.cpp:39-52).
  */
 LEVO_OPS_API int levo_channel_bias_add_f32(const float *in, const void *bias, int bias_dtype,
                                            float *out, int64_t channels, int64_t time,
@@ -119,8 +119,8 @@ LEVO_OPS_API int levo_channel_bias_add_f32(const float *in, const void *bias, in
  *   flags & LEVO_FUSED_TANH: y_out = tanh(y_out)
  * Covers every elementwise node of run_residual (src/levo-vae.cpp:90-101) and
  * the stage loop (src/levo-vae.cpp:212-235): conv bias add
- * (src/levo-audio-ops.cpp:74-87), residual add (src/levo-vae.cpp:100) and the
- * SnakeBeta that follows (src/levo-audio-ops.cpp:181-186).  The addition order
+ * (src/levo-audio-ops.cpp:39-52), residual add (src/levo-vae.cpp:100) and the
+ * SnakeBeta that follows (src/levo-audio-ops.cpp:146-151).  The addition order
  * is the reference graph's: residual + (conv + bias).
  */
 #define LEVO_FUSED_TANH 1u
@@ -223,7 +223,7 @@ LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topo
  * Same, with the packed parameters stored as IEEE F16 (the reference's F16 VAE
  * artifact, tools/levo-quantize.cpp:286-312): they stay F16 in HBM and every
  * fused unit promotes them to F32 in-kernel, as the reference's graph casts
- * each F16 weight to F32 before its node (src/levo-audio-ops.cpp:67-72).
+ * each F16 weight to F32 before its node (src/levo-audio-ops.cpp:32-37).
  */
 LEVO_OPS_API int levo_vae_chain_create_f16(levo_vae_chain **out, const levo_vae_topology *topology,
                                            const uint16_t *params_host, int64_t max_frames,
@@ -327,9 +327,11 @@ LEVO_OPS_API int levo_vae_chain_timing(levo_vae_chain *chain, levo_kernel_timing
  * process exits; the largest activation tensor of the window must fit in
  * 2^21 floats (the reference topology: frames <= 8), else LEVO_OPS_EINVAL.
  * Nothing is allocated: no cudaMalloc, no cudaFree, no events.
- * The first call on a device resolves the array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture.  All calls on a device share the array and it keeps the
+ * Each call made outside stream capture looks up the array's device address
+ * (cudaGetSymbolAddress) with the device current, so a device reset leaves no
+ * stale address; a call under capture uses the address of the last call outside
+ * it, so make the first call on a device before any stream capture.  All calls
+ * on a device share the array and it keeps the
  * previous call's contents (the decode writes every value before reading it,
  * so nothing needs clearing); calls that overlap on the GPU (other streams,
  * other threads) race on it.  flags: LEVO_CHAIN_TANH only.
@@ -436,14 +438,32 @@ LEVO_OPS_API int levo_flow_incontext_f32(float *state, const float *noise, const
  * One Euler step with the CFG combine fused (src/levo-flow-renderer.cpp:102-106,
  * 301-308):  v = cfg ? uncond + guidance*(cond - uncond) : uncond;  state += dt*v
  * where dt = 1/steps in F32.  `cond` is ignored (may be NULL) when cfg == 0.
- * `status` (optional device int32): bit 1 is set when a velocity value is not
- * finite, bit 2 when an updated state value is not finite (the reference's
- * require_finite checks, src/levo-flow-renderer.cpp:104,106).  The caller
- * clears it; the kernel only sets bits.
+ * `status` (optional device int32): bit value 1 is set when a velocity value is
+ * not finite, bit value 2 when an updated state value is not finite (the
+ * reference's require_finite checks, src/levo-flow-renderer.cpp:104,106).  The
+ * caller clears it; the kernel only sets bits.
  */
 LEVO_OPS_API int levo_euler_cfg_step_f32(float *state, const float *uncond, const float *cond,
                                          int64_t n, int32_t cfg, float guidance, int64_t steps,
                                          int32_t *status, levo_stream_t stream);
+
+/*
+ * Status word of the multi-step solves: the first failing step and its kind,
+ *   LEVO_EULER_STATUS(step, kind) = ((LEVO_EULER_STEP_LIMIT - step) << 2) | kind,
+ * kind LEVO_EULER_FAIL_VELOCITY (3: a combined velocity was not finite; as in
+ * levo_euler_cfg_step_f32 both bits are set, because the state would be too)
+ * or LEVO_EULER_FAIL_STATE (2: an updated state was not finite after a finite
+ * velocity).  Kernels combine them with atomicMax, so the word keeps the
+ * earliest step, and the velocity kind on a tie (the reference checks the
+ * velocity first, src/levo-flow-renderer.cpp:104,106).  0 = no failure.
+ */
+#define LEVO_EULER_STEP_LIMIT 268435456 /* 2^28: steps of a solve must stay below it */
+#define LEVO_EULER_FAIL_STATE 2
+#define LEVO_EULER_FAIL_VELOCITY 3
+#define LEVO_EULER_STATUS(step, kind) ((int32_t)((((int64_t)LEVO_EULER_STEP_LIMIT - (int64_t)(step)) << 2) | (kind)))
+#define LEVO_EULER_STATUS_STEP(status) \
+    (((status) >> 2) ? (int64_t)LEVO_EULER_STEP_LIMIT - (int64_t)((status) >> 2) : (int64_t)-1)
+#define LEVO_EULER_STATUS_KIND(status) ((status) & 3)
 
 /*
  * Fused multi-step solve for velocities known up front (benchmarks, replay of
@@ -454,7 +474,13 @@ LEVO_OPS_API int levo_euler_cfg_step_f32(float *state, const float *uncond, cons
  * uncond / cond are [count][batch][row] (velocity of step first_step + k at k).
  * Stopping after `count` steps gives the reference's durable per-step resume
  * boundary (src/levo-flow-renderer.cpp:74-88,107-110).
- * status: as levo_euler_cfg_step_f32.
+ * `status` (optional device int32, cleared by the caller): the first failing
+ * step and kind as LEVO_EULER_STATUS.  An element whose velocity or state goes
+ * non-finite stops there, keeping its state after the last step it completed,
+ * and the context restore is skipped for it; elements that did not fail run
+ * every step.  levo_cfg_euler_solve_f32 gives the reference's exact checkpoint
+ * for the whole state instead.  steps >= LEVO_EULER_STEP_LIMIT:
+ * LEVO_OPS_EUNSUPPORTED.
  */
 LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, const float *context,
                                           const float *uncond, const float *cond,
@@ -462,6 +488,67 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
                                           int64_t first_step, int64_t count, int64_t steps,
                                           int32_t cfg, float guidance, float sigma_min,
                                           int32_t *status, levo_stream_t stream);
+
+/*
+ * solve_flow_euler over velocities known up front, with its error semantics
+ * (src/levo-flow-renderer.cpp:57-120): runs steps [first_step, first_step +
+ * count) as levo_cfg_euler_multi_f32 and, when some step's combined velocity
+ * (:104) or updated state (:106) holds a non-finite value, stops where the
+ * reference throws: `state` is left at the reference's checkpoint (every
+ * element after the steps completed before that step, the checkpoint the
+ * reference writes at :107-110), *completed_steps receives that step, and the
+ * call returns LEVO_OPS_ENONFINITE with the reference's message ("Euler velocity
+ * contains a non-finite value" / "Euler state contains a non-finite value").
+ * On success *completed_steps = first_step + count.  All batch rows form one
+ * solve: they stop together.
+ * checkpoint: caller-owned device scratch of batch * row F32 (the state before
+ * the call, kept to replay the completed steps after a failure); status: a
+ * caller-owned device int32 (receives LEVO_EULER_STATUS).  Synchronous: the
+ * call waits for `stream` before it returns.
+ */
+LEVO_OPS_API int levo_cfg_euler_solve_f32(float *state, const float *noise, const float *context,
+                                          const float *uncond, const float *cond,
+                                          int64_t batch, int64_t row, int64_t prefix,
+                                          int64_t first_step, int64_t count, int64_t steps,
+                                          int32_t cfg, float guidance, float sigma_min,
+                                          float *checkpoint, int32_t *status, int64_t *completed_steps,
+                                          levo_stream_t stream);
+
+/*
+ * Velocity callback of levo_flow_euler_solve_f32 (the estimator evaluation of
+ * solve_flow_euler's velocity callback, src/levo-flow-renderer.cpp:102):
+ * given the device state the estimator sees at `step` (time = step / steps),
+ * returns a device pointer to the velocity, [2][n] F32 (row 0 unconditional,
+ * row 1 conditional) when the solve combines CFG, else [n]; NULL reports a
+ * failure.  Work it enqueues on `stream` is ordered before the update.
+ */
+typedef const float *(*levo_velocity_fn)(void *user, const float *state, int64_t step, float time,
+                                         levo_stream_t stream);
+
+/*
+ * solve_flow_euler (src/levo-flow-renderer.cpp:57-120) on a device state
+ * [frames][latent_dim], one velocity evaluation per step: for each step from
+ * first_step (a resume point, :76-84) to steps - 1 it polls `cancel`, applies
+ * the in-context interpolation (:93-101), calls `velocity`, and runs the fused
+ * CFG combine + Euler update with the reference's finiteness checks
+ * (:104,106), reading the status back after each step; after the last step it
+ * restores the context prefix (:113-114).
+ * checkpoint (optional device [frames * latent_dim] F32): the state before each
+ * step is kept there, so that on a non-finite velocity or state the solve
+ * leaves `state` at the reference's checkpoint (:107-110) and returns
+ * LEVO_OPS_ENONFINITE with the reference's message; without it the state is
+ * left as the failing step's update wrote it.  status: caller-owned device
+ * int32 scratch.  *completed_steps (host) receives the steps completed (the
+ * resume point after a failure or a cancellation, `steps` on success).
+ * cancel (optional) returning non-zero: LEVO_OPS_ECANCELLED with the state at
+ * the last completed step.  Synchronises `stream` once per step.
+ */
+LEVO_OPS_API int levo_flow_euler_solve_f32(float *state, const float *noise, const float *context,
+                                           int64_t frames, int64_t latent_dim, int64_t incontext_frames,
+                                           float sigma_min, int64_t steps, int64_t first_step, int32_t cfg,
+                                           float guidance, levo_velocity_fn velocity, void *velocity_user,
+                                           levo_cancel_fn cancel, void *cancel_user, float *checkpoint,
+                                           int32_t *status, int64_t *completed_steps, levo_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* next (f2)  latent normalisation and the layout change into the VAE         */
@@ -489,7 +576,7 @@ LEVO_OPS_API int levo_latent_normalize_f32(const float *raw, const float *mean, 
 /* ------------------------------------------------------------------------- */
 /*
  * Replaces Sampler::sample_streams with use_sampling = false
- * (src/levo-sampling.cpp:127-154, sample_top_k_counted :74-97): for each row
+ * (src/levo-sampling.cpp:129-152, sample_top_k_counted :75-97): for each row
  * (stream) of `vocab` logits (row stride ld),
  *   1. each distinct id of recent[row][0..recent_len) in [0, penalty_limit)
  *      divides its logit once by `penalty` (:39-48; penalty_limit <= 0 means

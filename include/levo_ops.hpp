@@ -4,7 +4,10 @@
 // the error behaviour of the reference's operators, so a call site in
 // LeVo2.cpp changes its arguments (device pointers instead of ggml_tensor*),
 // not its structure or its exception handling:
-//   invalid arguments  -> std::invalid_argument("LeVo audio graph: ...")   (src/levo-audio-ops.cpp:45-47)
+//   invalid arguments  -> std::invalid_argument("LeVo audio graph: ...")   (src/levo-audio-ops.cpp:10-12)
+//   norm failures      -> std::runtime_error("LeVo LM: ...") for RMSNorm    (src/levo-lm.cpp:50-52),
+//                         std::runtime_error("LeVo Flow estimator: ...") for LayerNorm
+//                                                                          (src/levo-flow-estimator.cpp:35-37)
 //   Flow-side checks   -> std::invalid_argument with the reference's wording (src/levo-renderer-pattern.cpp:127-130)
 //   non-finite Euler   -> std::runtime_error("LeVo Flow renderer: ...")    (src/levo-flow-renderer.cpp:13-15,24-28)
 //   cancellation       -> levo::b200::operation_cancelled                 (include/levo.h:21-24)
@@ -16,10 +19,12 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <exception>
 #include <functional>
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "levo_ops.h"
@@ -39,12 +44,21 @@ inline void check(int rc, const char *domain) {
     if (rc == LEVO_OPS_ECANCELLED) throw operation_cancelled();
     throw std::runtime_error(msg);
 }
+// The reference's LM and Flow estimator report every failure (shapes included)
+// through their own fail(), as std::runtime_error with their own prefix.
+inline void check_runtime(int rc, const char *domain) {
+    if (rc == LEVO_OPS_OK) return;
+    if (rc == LEVO_OPS_ECANCELLED) throw operation_cancelled();
+    throw std::runtime_error(std::string(domain) + levo_ops_last_error());
+}
 constexpr const char *kAudio = "LeVo audio graph: ";
+constexpr const char *kLm = "LeVo LM: ";
+constexpr const char *kFlowEstimator = "LeVo Flow estimator: ";
 constexpr const char *kFlow = "LeVo Flow renderer: ";
 constexpr const char *kVae = "LeVo VAE: ";
 }  // namespace detail
 
-// levo::detail::snake_beta (src/levo-audio-ops.cpp:160-187): y = x + sin(x*e^a)^2 / (e^b + 1e-9).
+// levo::detail::snake_beta (src/levo-audio-ops.cpp:125-152): y = x + sin(x*e^a)^2 / (e^b + 1e-9).
 inline void snake_beta(const float *x, const float *alpha_log, const float *beta_log, float *y,
                        int64_t channels, int64_t time, levo_stream_t stream = nullptr) {
     detail::check(levo_snakebeta_f32(x, time, alpha_log, beta_log, LEVO_DTYPE_F32, y, time, channels, time,
@@ -76,17 +90,17 @@ inline void fused_unit(const levo_fused_unit &unit, levo_stream_t stream = nullp
 inline void add_rms_norm_f16(const void *x, const void *residual, const float *gamma, void *h_out, void *y_out,
                              int64_t rows, int64_t dim, float eps, bool f16_boundary,
                              levo_stream_t stream = nullptr) {
-    detail::check(levo_add_rmsnorm_f16(x, residual, gamma, h_out, y_out, rows, dim, eps,
-                                       f16_boundary ? LEVO_NORM_F16_BOUNDARY : 0u, stream),
-                  detail::kAudio);
+    detail::check_runtime(levo_add_rmsnorm_f16(x, residual, gamma, h_out, y_out, rows, dim, eps,
+                                               f16_boundary ? LEVO_NORM_F16_BOUNDARY : 0u, stream),
+                          detail::kLm);
 }
 
 // layer_norm + residual add (src/levo-flow-estimator.cpp:106-109,221-227), F32 activations.
 inline void add_layer_norm_f32(const float *x, const float *residual, const float *gamma, const float *beta,
                                float *h_out, float *y_out, int64_t rows, int64_t dim, float eps = 1.0e-5f,
                                levo_stream_t stream = nullptr) {
-    detail::check(levo_add_layernorm_f32(x, residual, gamma, beta, h_out, y_out, rows, dim, eps, 0u, stream),
-                  detail::kAudio);
+    detail::check_runtime(levo_add_layernorm_f32(x, residual, gamma, beta, h_out, y_out, rows, dim, eps, 0u, stream),
+                          detail::kFlowEstimator);
 }
 
 // combine_renderer_cfg (src/levo-renderer-pattern.cpp:123-135), device vectors.
@@ -101,11 +115,20 @@ inline void combine_renderer_cfg(const float *unconditional, const float *condit
     detail::check(rc, detail::kFlow);
 }
 
-// One step of solve_flow_euler (src/levo-flow-renderer.cpp:93-106) on device
-// state [frames][latent_dim]: in-context interpolation, then the caller's
-// velocity callback (the estimator), then the fused CFG + Euler update.  The
-// velocity callback returns a device pointer to [2][frames*latent_dim]
-// (row 0 unconditional, row 1 conditional) when cfg, else [frames*latent_dim].
+// solve_flow_euler (src/levo-flow-renderer.cpp:57-120) on device state
+// [frames][latent_dim]: per step the in-context interpolation, the caller's
+// velocity callback (the estimator), the fused CFG combine + Euler update and
+// the reference's finiteness checks, then the final context restore; the work
+// runs in levo_flow_euler_solve_f32.  `velocity(state, step)` returns a device
+// pointer to [2][frames*latent_dim] (row 0 unconditional, row 1 conditional)
+// when cfg, else [frames*latent_dim]; `cancelled()` is polled before each step.
+// Errors carry the reference's exception types and messages: a non-finite
+// velocity / state or an invalid input throws std::runtime_error("LeVo Flow
+// renderer: ..."), cancellation operation_cancelled; an exception thrown by a
+// callback propagates unchanged.  With a checkpoint (the reference's
+// euler_resume_state, its state a caller-owned device buffer), the solve keeps
+// the state before each step there: after a failure or a cancellation `state`
+// holds the reference's resume state and checkpoint->completed_steps its step.
 struct euler_device_input {
     float *state;              // in/out
     const float *noise;        // [frames*latent_dim]
@@ -116,35 +139,59 @@ struct euler_device_input {
     float sigma_min = 1.0e-4f;
 };
 
+struct euler_device_checkpoint {
+    float *state = nullptr;  // device [frames*latent_dim], caller-owned
+    int64_t completed_steps = 0;
+};
+
 template <class Velocity, class Cancelled>
 void solve_flow_euler(const euler_device_input &in, int64_t steps, bool cfg, float guidance,
                       Velocity &&velocity, Cancelled &&cancelled, int32_t *status_dev,
-                      int64_t completed_steps = 0, levo_stream_t stream = nullptr) {
-    if (steps <= 0) throw std::runtime_error("LeVo Flow renderer: Euler step count must be positive");
-    if (in.incontext_frames > in.frames)
-        throw std::runtime_error("LeVo Flow renderer: Euler in-context length exceeds frame count");
-    const int64_t n = in.frames * in.latent_dim;
-    for (int64_t step = completed_steps; step < steps; ++step) {
-        if (cancelled()) throw operation_cancelled();
-        if (in.incontext_frames > 0)
-            detail::check(levo_flow_incontext_f32(in.state, in.noise, in.context, 1, n,
-                                                  in.incontext_frames * in.latent_dim, step, steps, in.sigma_min,
-                                                  stream),
-                          detail::kFlow);
-        const float *v = velocity(static_cast<const float *>(in.state), step);
-        detail::check(levo_euler_cfg_step_f32(in.state, v, cfg ? v + n : nullptr, n, cfg ? 1 : 0, guidance, steps,
-                                              status_dev, stream),
-                      detail::kFlow);
-    }
-    // Final context restore (src/levo-flow-renderer.cpp:113-114): a zero-step
-    // multi-step call at the end of the solve restores the prefix only.
-    detail::check(levo_cfg_euler_multi_f32(in.state, in.noise, in.context, nullptr, nullptr, 1, n,
-                                           in.incontext_frames * in.latent_dim, steps, 0, steps, 0, 1.0f,
-                                           in.sigma_min, nullptr, stream),
-                  detail::kFlow);
+                      int64_t completed_steps = 0, levo_stream_t stream = nullptr,
+                      euler_device_checkpoint *checkpoint = nullptr) {
+    using V = std::remove_reference_t<Velocity>;
+    using C = std::remove_reference_t<Cancelled>;
+    struct callbacks {
+        V *velocity;
+        C *cancelled;
+        std::exception_ptr error;
+    } cb{&velocity, &cancelled, nullptr};
+    const levo_velocity_fn on_velocity = [](void *user, const float *state, int64_t step, float,
+                                            levo_stream_t) -> const float * {
+        auto *c = static_cast<callbacks *>(user);
+        try {
+            return (*c->velocity)(state, step);
+        } catch (...) {
+            c->error = std::current_exception();
+            return nullptr;
+        }
+    };
+    const levo_cancel_fn on_cancel = [](void *user) -> int {
+        auto *c = static_cast<callbacks *>(user);
+        try {
+            return (*c->cancelled)() ? 1 : 0;
+        } catch (...) {
+            c->error = std::current_exception();
+            return 1;
+        }
+    };
+    int64_t done = completed_steps;
+    const int rc = levo_flow_euler_solve_f32(in.state, in.noise, in.context, in.frames, in.latent_dim,
+                                             in.incontext_frames, in.sigma_min, steps, completed_steps, cfg ? 1 : 0,
+                                             guidance, on_velocity, &cb, on_cancel, &cb,
+                                             checkpoint ? checkpoint->state : nullptr, status_dev, &done, stream);
+    if (checkpoint) checkpoint->completed_steps = done;
+    if (cb.error) std::rethrow_exception(cb.error);
+    if (rc == LEVO_OPS_OK) return;
+    if (rc == LEVO_OPS_ECANCELLED) throw operation_cancelled();
+    std::string msg = levo_ops_last_error();
+    const std::string own = "levo_flow_euler_solve_f32: ";
+    if (msg.rfind(own, 0) == 0) msg.erase(0, own.size());
+    if (rc == LEVO_OPS_ENONFINITE) msg.erase(msg.find(" (step"));  // the reference names no step
+    throw std::runtime_error(std::string(detail::kFlow) + msg);
 }
 
-// vae_decode_result (src/levo-vae.h:13-19).
+// vae_decode_result (src/levo-vae.h:12-19).
 struct vae_decode_result {
     std::size_t frames = 0;
     std::size_t samples_per_channel = 0;

@@ -146,7 +146,7 @@ __device__ __forceinline__ float load_param(const void *p, int64_t i, int dtype)
     return static_cast<const float *>(p)[i];
 }
 
-// SnakeBeta of the reference graph (src/levo-audio-ops.cpp:181-186):
+// SnakeBeta of the reference graph (src/levo-audio-ops.cpp:146-151):
 //   alpha = exp(alpha_log), beta = exp(beta_log)*1 + 1e-9, y = x + sin(x*alpha)^2 / beta.
 // Per channel the kernels stage alpha and 1/beta (IEEE reciprocal of the
 // reference's beta); per element they evaluate y = fma(sin^2(x*alpha), 1/beta, x).

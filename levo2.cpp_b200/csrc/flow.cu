@@ -10,9 +10,15 @@
 //            t = step * dt, ns = 1 - (1 - sigma_min) * t
 //                                             (src/levo-flow-renderer.cpp:93-101)
 // The reference's finiteness checks (src/levo-flow-renderer.cpp:104,106) become
-// bits in an optional device status word.
+// an optional device status word.  The per-step kernel ORs the failure kinds
+// into it; the multi-step kernels record the first failing step (the one the
+// reference throws at) with atomicMax on LEVO_EULER_STATUS(step, kind), and an
+// element stops updating at its first failure, keeping its state after the
+// last step it completed.
 #include <algorithm>
+#include <climits>
 #include <cmath>
+#include <string>
 
 #include "common.cuh"
 
@@ -38,6 +44,12 @@ __device__ __forceinline__ void prefix_times(int64_t step, float dt, float sigma
 
 __device__ __forceinline__ void flag_status(int32_t *status, int bits) {
     if (status && bits) atomicOr(status, bits);
+}
+
+// The earliest failing step wins; on a tie the velocity kind (3 > 2), which the
+// reference checks before the state.
+__device__ __forceinline__ void record_failure(int32_t *status, int64_t step, int kind) {
+    if (status) atomicMax(status, static_cast<int32_t>(LEVO_EULER_STATUS(step, kind)));
 }
 
 struct CfgArgs {
@@ -150,14 +162,14 @@ struct MultiArgs {
 __global__ void __launch_bounds__(kThreads) euler_multi_kernel(const MultiArgs a) {
     const int64_t n = a.batch * a.row;
     const float dt = step_dt(a.steps);
-    int bits = 0;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const bool in_prefix = (i % a.row) < a.prefix;
         float x = a.state[i];
         const float nz = in_prefix ? a.noise[i] : 0.f;
         const float cx = in_prefix ? a.ctx[i] : 0.f;
-        for (int64_t k0 = 0; k0 < a.count; k0 += kStepChunk) {
+        bool failed = false;
+        for (int64_t k0 = 0; k0 < a.count && !failed; k0 += kStepChunk) {
             float uu[kStepChunk], cc[kStepChunk];
 #pragma unroll
             for (int j = 0; j < kStepChunk; ++j) {
@@ -169,89 +181,141 @@ __global__ void __launch_bounds__(kThreads) euler_multi_kernel(const MultiArgs a
 #pragma unroll
             for (int j = 0; j < kStepChunk; ++j) {
                 if (k0 + j >= a.count) break;
+                const int64_t step = a.first + k0 + j;
+                float xs = x;
                 if (in_prefix) {
                     float t, ns;
-                    prefix_times(a.first + k0 + j, dt, a.sigma_min, t, ns);
-                    x = __fadd_rn(__fmul_rn(ns, nz), __fmul_rn(t, cx));
+                    prefix_times(step, dt, a.sigma_min, t, ns);
+                    xs = __fadd_rn(__fmul_rn(ns, nz), __fmul_rn(t, cx));
                 }
                 const float v = a.cfg ? cfg_mix(uu[j], cc[j], a.g) : uu[j];
-                if (!isfinite(v)) bits |= 1;
-                x = __fadd_rn(x, __fmul_rn(dt, v));
-                if (!isfinite(x)) bits |= 2;
+                if (!isfinite(v)) {
+                    record_failure(a.status, step, 3);
+                    failed = true;
+                    break;
+                }
+                const float nx = __fadd_rn(xs, __fmul_rn(dt, v));
+                if (!isfinite(nx)) {
+                    record_failure(a.status, step, 2);
+                    failed = true;
+                    break;
+                }
+                x = nx;
             }
         }
-        if (in_prefix && a.first + a.count == a.steps) x = cx;
+        if (!failed && in_prefix && a.first + a.count == a.steps) x = cx;
         a.state[i] = x;
     }
-    flag_status(a.status, bits);
 }
 
-// Staged form: a CTA of kStagedThreads threads owns kStagedThreads consecutive
-// elements; the velocities of up to kStagedSteps steps for them are copied into
-// shared memory with cp.async in one burst (all of config 2's 13 MB is in
-// flight at once), then each thread runs its steps from shared memory.
-constexpr int kStagedThreads = 64;
+// Staged form.  A CTA owns kStagedElems consecutive elements; its 256 threads
+// copy the velocities of up to kStagedSteps steps for them into shared memory
+// with cp.async in one burst (all of config 2's 13 MB is in flight at once).
+// Then, per round:
+//   velocity phase: four threads per element (steps q, q + 4, ...) form the CFG
+//     combine, note the first non-finite velocity and replace u by dt * v in
+//     place (the reference rounds dt * v before adding it, so x + w is its
+//     x + dt * v bit for bit);
+//   chain phase: one thread per element runs the dependent x = x + w (after
+//     the in-context interpolation for prefix elements) up to that step.
+// Outside the prefix a non-finite state stays non-finite (w is finite), so the
+// chain checks the state once at the end and replays the round with per-step
+// checks only when it failed; prefix elements, re-interpolated every step,
+// check every step.
+constexpr int kStagedElems = 64;
+constexpr int kStagedLanes = 4;
+constexpr int kStagedThreads = kStagedElems * kStagedLanes;
 constexpr int kStagedSteps = 64;
 
 __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(const MultiArgs a) {
-    extern __shared__ float4 stage[];  // [2][steps][kStagedThreads/4] float4
+    extern __shared__ float4 stage[];  // [2][kStagedSteps][kStagedElems] F32: u (then dt * v), c
+    __shared__ int vfirst[kStagedElems];
+    float *su = reinterpret_cast<float *>(stage);
+    float *sc = su + kStagedSteps * kStagedElems;
     const int64_t n = a.batch * a.row;
-    const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kStagedThreads;
-    const int64_t i = i0 + threadIdx.x;
-    const bool active = i < n;
-    const int per_step = kStagedThreads / 4;  // float4 chunks per step and array
+    const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kStagedElems;
+    const int tid = threadIdx.x;
+    const int e = tid % kStagedElems;  // element of the velocity phase
+    const int q = tid / kStagedElems;  // its step lane
+    const int64_t i = i0 + tid;        // element of the chain phase (threads < kStagedElems)
+    const bool active = tid < kStagedElems && i < n;
+    // n % 4 == 0 (launcher), so this CTA's elements are whole 16-byte chunks
+    const int valid = static_cast<int>(n - i0 < kStagedElems ? n - i0 : kStagedElems);
+    const int chunks_valid = valid / 4;
+    constexpr int kChunksPerStep = kStagedElems / 4;
     const float dt = step_dt(a.steps);
-    int bits = 0;
     const bool in_prefix = active && (i % a.row) < a.prefix;
     float x = active ? a.state[i] : 0.f;
     const float nz = in_prefix ? a.noise[i] : 0.f;
     const float cx = in_prefix ? a.ctx[i] : 0.f;
-    const int64_t full = (n - i0) >= kStagedThreads ? per_step : (n - i0 + 3) / 4;
+    bool failed = false;
     for (int64_t k0 = 0; k0 < a.count; k0 += kStagedSteps) {
         const int cnt = static_cast<int>(a.count - k0 < kStagedSteps ? a.count - k0 : kStagedSteps);
-        __syncthreads();  // the previous chunk has been consumed
-        // Thread t copies chunk (t % per_step) of steps t / per_step, + kGroups, ...
-        // for both arrays: no division inside the loop.
+        __syncthreads();  // the previous round has been consumed
+        if (tid < kStagedElems) vfirst[tid] = INT_MAX;
         {
-            constexpr int kGroups = kStagedThreads / (kStagedThreads / 4);  // step rows copied per pass
-            const int ch = threadIdx.x % per_step;
-            const int st0 = threadIdx.x / per_step;
-            if (ch < full) {
-                const float *ub = a.u + (k0 + st0) * n + i0 + ch * 4;
-                const float *cb = a.cfg ? a.c + (k0 + st0) * n + i0 + ch * 4 : nullptr;
-                for (int st = st0; st < cnt; st += kGroups) {
-                    cp_async16(stage + st * per_step + ch, ub);
-                    if (a.cfg) cp_async16(stage + (kStagedSteps + st) * per_step + ch, cb);
-                    ub += kGroups * n;
-                    if (a.cfg) cb += kGroups * n;
+            const int per_array = cnt * kChunksPerStep;
+            const int total = a.cfg ? 2 * per_array : per_array;
+            for (int idx = tid; idx < total; idx += kStagedThreads) {
+                const bool second = idx >= per_array;
+                const int rem = second ? idx - per_array : idx;
+                const int st = rem / kChunksPerStep;
+                const int ch = rem % kChunksPerStep;
+                if (ch < chunks_valid) {
+                    const float *src = (second ? a.c : a.u) + (k0 + st) * n + i0 + ch * 4;
+                    cp_async16((second ? sc : su) + st * kStagedElems + ch * 4, src);
                 }
             }
         }
         cp_async_wait_all();
         __syncthreads();
-        if (active) {
-            const float *su = reinterpret_cast<const float *>(stage);
-            const float *sc = su + kStagedSteps * kStagedThreads;
-#pragma unroll 10
-            for (int j = 0; j < cnt; ++j) {
-                if (in_prefix) {
-                    float t, ns;
-                    prefix_times(a.first + k0 + j, dt, a.sigma_min, t, ns);
-                    x = __fadd_rn(__fmul_rn(ns, nz), __fmul_rn(t, cx));
+        if (e < valid) {
+            for (int st = q; st < cnt; st += kStagedLanes) {
+                const float u = su[st * kStagedElems + e];
+                const float v = a.cfg ? cfg_mix(u, sc[st * kStagedElems + e], a.g) : u;
+                if (!isfinite(v)) atomicMin(&vfirst[e], st);
+                su[st * kStagedElems + e] = __fmul_rn(dt, v);
+            }
+        }
+        __syncthreads();
+        if (active && !failed) {
+            const int kv = vfirst[tid];
+            const int run = kv < cnt ? kv : cnt;
+            int fail_st = kv < cnt ? kv : -1;
+            int kind = 3;
+            const float x0 = x;
+            if (!in_prefix) {
+#pragma unroll 8
+                for (int st = 0; st < run; ++st) x = __fadd_rn(x, su[st * kStagedElems + tid]);
+            }
+            if (in_prefix || !isfinite(x)) {
+                x = x0;
+                for (int st = 0; st < run; ++st) {
+                    float xs = x;
+                    if (in_prefix) {
+                        float t, ns;
+                        prefix_times(a.first + k0 + st, dt, a.sigma_min, t, ns);
+                        xs = __fadd_rn(__fmul_rn(ns, nz), __fmul_rn(t, cx));
+                    }
+                    const float nx = __fadd_rn(xs, su[st * kStagedElems + tid]);
+                    if (!isfinite(nx)) {
+                        fail_st = st;
+                        kind = 2;
+                        break;
+                    }
+                    x = nx;
                 }
-                const float u = su[j * kStagedThreads + threadIdx.x];
-                const float v = a.cfg ? cfg_mix(u, sc[j * kStagedThreads + threadIdx.x], a.g) : u;
-                if (!isfinite(v)) bits |= 1;
-                x = __fadd_rn(x, __fmul_rn(dt, v));
-                if (!isfinite(x)) bits |= 2;
+            }
+            if (fail_st >= 0) {
+                failed = true;
+                record_failure(a.status, a.first + k0 + fail_st, kind);
             }
         }
     }
     if (active) {
-        if (in_prefix && a.first + a.count == a.steps) x = cx;
+        if (!failed && in_prefix && a.first + a.count == a.steps) x = cx;
         a.state[i] = x;
     }
-    flag_status(a.status, bits);
 }
 
 int64_t grid_for(int64_t items) {
@@ -353,6 +417,8 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
                          "levo_cfg_euler_multi_f32: Euler in-context length exceeds frame count");
     if (first_step < 0 || count < 0 || first_step > steps || count > steps - first_step)
         return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: Euler resume step exceeds total steps");
+    if (steps >= LEVO_EULER_STEP_LIMIT)
+        return set_error(LEVO_OPS_EUNSUPPORTED, "levo_cfg_euler_multi_f32: Euler step count above the status limit");
     if (!std::isfinite(sigma_min) || sigma_min <= 0.f)
         return set_error(LEVO_OPS_EINVAL,
                          "levo_cfg_euler_multi_f32: Euler sigma_min must be finite and positive");
@@ -365,19 +431,162 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
     const MultiArgs a{state, noise, context, uncond, cond, batch, row, prefix, first_step,
                       count, steps, cfg ? 1 : 0, guidance, sigma_min, status};
     const int64_t n = batch * row;
-    // one staged CTA per kStagedThreads elements: the grid must fit in 2^31 - 1 blocks
+    // one staged CTA per kStagedElems elements: the grid must fit in 2^31 - 1 blocks
     const bool staged = count > 0 && n % 4 == 0 && aligned_to(uncond, 16) && (!cfg || aligned_to(cond, 16)) &&
-                        (n + kStagedThreads - 1) / kStagedThreads <= 0x7fffffff;
+                        (n + kStagedElems - 1) / kStagedElems <= 0x7fffffff;
     if (staged) {
-        // [2][kStagedSteps][kStagedThreads] F32 = 32 KB of shared memory
-        const size_t smem = 2 * kStagedSteps * kStagedThreads * sizeof(float);
-        euler_multi_staged_kernel<<<static_cast<unsigned>((n + kStagedThreads - 1) / kStagedThreads),
+        // [2][kStagedSteps][kStagedElems] F32 = 32 KB of shared memory
+        const size_t smem = 2 * kStagedSteps * kStagedElems * sizeof(float);
+        euler_multi_staged_kernel<<<static_cast<unsigned>((n + kStagedElems - 1) / kStagedElems),
                                     kStagedThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a);
     } else {
         euler_multi_kernel<<<static_cast<unsigned>(grid_for(n)), kThreads, 0,
                              reinterpret_cast<cudaStream_t>(stream)>>>(a);
     }
     return check_launch("levo_cfg_euler_multi_f32");
+}
+
+LEVO_OPS_API int levo_cfg_euler_solve_f32(float *state, const float *noise, const float *context,
+                                          const float *uncond, const float *cond, int64_t batch,
+                                          int64_t row, int64_t prefix, int64_t first_step,
+                                          int64_t count, int64_t steps, int32_t cfg,
+                                          float guidance, float sigma_min, float *checkpoint,
+                                          int32_t *status, int64_t *completed_steps,
+                                          levo_stream_t stream) {
+    using namespace levo;
+    clear_error();
+    const char *w = "levo_cfg_euler_solve_f32";
+    if (checkpoint == nullptr || status == nullptr || completed_steps == nullptr)
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": checkpoint, status and completed_steps are required");
+    if (!aligned_to(checkpoint, 4) || !aligned_to(status, 4))
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": pointer is not 4-byte aligned");
+    if (state == nullptr || batch <= 0 || row <= 0)
+        return set_error(LEVO_OPS_EINVAL, std::string(w) + ": Euler state dimensions must be positive");
+    *completed_steps = first_step;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t bytes = static_cast<size_t>(batch * row) * sizeof(float);
+    // the checkpoint of the call's start, then the fused steps
+    cudaError_t err = cudaMemcpyAsync(checkpoint, state, bytes, cudaMemcpyDeviceToDevice, s);
+    if (err == cudaSuccess) err = cudaMemsetAsync(status, 0, sizeof(int32_t), s);
+    if (err != cudaSuccess) return set_error(LEVO_OPS_ECUDA, std::string(w) + ": " + cudaGetErrorString(err));
+    int rc = levo_cfg_euler_multi_f32(state, noise, context, uncond, cond, batch, row, prefix, first_step, count,
+                                      steps, cfg, guidance, sigma_min, status, stream);
+    if (rc != LEVO_OPS_OK) {
+        cudaStreamSynchronize(s);
+        return rc;
+    }
+    int32_t word = 0;
+    err = cudaMemcpyAsync(&word, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return set_error(LEVO_OPS_ECUDA, std::string(w) + ": " + cudaGetErrorString(err));
+    if (word == 0) {
+        *completed_steps = first_step + count;
+        return LEVO_OPS_OK;
+    }
+    // Some element failed at step `fail`: every element goes back to the call's
+    // start and replays the steps before it (they were finite for all), which
+    // is the reference's checkpoint of the last completed step.
+    const int64_t fail = LEVO_EULER_STATUS_STEP(word);
+    const int kind = LEVO_EULER_STATUS_KIND(word);
+    if (fail < first_step || fail >= first_step + count)
+        return set_error(LEVO_OPS_ECUDA, std::string(w) + ": inconsistent status word");
+    err = cudaMemcpyAsync(state, checkpoint, bytes, cudaMemcpyDeviceToDevice, s);
+    if (err != cudaSuccess) return set_error(LEVO_OPS_ECUDA, std::string(w) + ": " + cudaGetErrorString(err));
+    if (fail > first_step) {
+        rc = levo_cfg_euler_multi_f32(state, noise, context, uncond, cond, batch, row, prefix, first_step,
+                                      fail - first_step, steps, cfg, guidance, sigma_min, nullptr, stream);
+        if (rc != LEVO_OPS_OK) {
+            cudaStreamSynchronize(s);
+            return rc;
+        }
+    }
+    err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return set_error(LEVO_OPS_ECUDA, std::string(w) + ": " + cudaGetErrorString(err));
+    *completed_steps = fail;
+    return set_error(LEVO_OPS_ENONFINITE,
+                     std::string(w) + (kind == LEVO_EULER_FAIL_VELOCITY ? ": Euler velocity" : ": Euler state") +
+                         " contains a non-finite value (step " + std::to_string(fail) + ")");
+}
+
+LEVO_OPS_API int levo_flow_euler_solve_f32(float *state, const float *noise, const float *context,
+                                           int64_t frames, int64_t latent_dim, int64_t incontext_frames,
+                                           float sigma_min, int64_t steps, int64_t first_step, int32_t cfg,
+                                           float guidance, levo_velocity_fn velocity, void *velocity_user,
+                                           levo_cancel_fn cancel, void *cancel_user, float *checkpoint,
+                                           int32_t *status, int64_t *completed_steps, levo_stream_t stream) {
+    using namespace levo;
+    clear_error();
+    const std::string w = "levo_flow_euler_solve_f32";
+    if (completed_steps == nullptr || status == nullptr || velocity == nullptr)
+        return set_error(LEVO_OPS_EINVAL, w + ": velocity, status and completed_steps are required");
+    *completed_steps = first_step;
+    // the reference's input checks (src/levo-flow-renderer.cpp:63-70)
+    if (steps <= 0) return set_error(LEVO_OPS_EINVAL, w + ": Euler step count must be positive");
+    if (frames <= 0 || latent_dim <= 0)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler state dimensions must be positive");
+    if (incontext_frames < 0 || incontext_frames > frames)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler in-context length exceeds frame count");
+    if (!std::isfinite(sigma_min) || sigma_min <= 0.f)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler sigma_min must be finite and positive");
+    if (first_step < 0 || first_step > steps)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler resume step exceeds total steps");
+    if (state == nullptr || noise == nullptr || context == nullptr)
+        return set_error(LEVO_OPS_EINVAL, w + ": required pointer is null");
+    if (cfg && !std::isfinite(guidance)) return set_error(LEVO_OPS_EINVAL, w + ": CFG guidance scale must be finite");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t n = frames * latent_dim;
+    const int64_t prefix = incontext_frames * latent_dim;
+    const size_t bytes = static_cast<size_t>(n) * sizeof(float);
+    const float dt = 1.0f / static_cast<float>(steps);
+    auto cuda_error = [&](cudaError_t err) {
+        return set_error(LEVO_OPS_ECUDA, w + ": " + cudaGetErrorString(err));
+    };
+    for (int64_t step = first_step; step < steps; ++step) {
+        if (cancel != nullptr && cancel(cancel_user) != 0) {
+            cudaStreamSynchronize(s);
+            return set_error(LEVO_OPS_ECANCELLED, w + ": cancelled before step " + std::to_string(step));
+        }
+        cudaError_t err = cudaSuccess;
+        if (checkpoint != nullptr) err = cudaMemcpyAsync(checkpoint, state, bytes, cudaMemcpyDeviceToDevice, s);
+        if (err == cudaSuccess) err = cudaMemsetAsync(status, 0, sizeof(int32_t), s);
+        if (err != cudaSuccess) return cuda_error(err);
+        int rc = LEVO_OPS_OK;
+        if (prefix > 0)
+            rc = levo_flow_incontext_f32(state, noise, context, 1, n, prefix, step, steps, sigma_min, stream);
+        if (rc != LEVO_OPS_OK) return rc;
+        const float time = static_cast<float>(step) * dt;
+        const float *v = velocity(velocity_user, state, step, time, stream);
+        if (v == nullptr) {
+            if (checkpoint != nullptr) cudaMemcpyAsync(state, checkpoint, bytes, cudaMemcpyDeviceToDevice, s);
+            cudaStreamSynchronize(s);
+            return set_error(LEVO_OPS_ECUDA, w + ": velocity callback failed at step " + std::to_string(step));
+        }
+        rc = levo_euler_cfg_step_f32(state, v, cfg ? v + n : nullptr, n, cfg, guidance, steps, status, stream);
+        if (rc != LEVO_OPS_OK) return rc;
+        int32_t word = 0;
+        err = cudaMemcpyAsync(&word, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+        if (err != cudaSuccess) return cuda_error(err);
+        if (word != 0) {
+            if (checkpoint != nullptr) {
+                err = cudaMemcpyAsync(state, checkpoint, bytes, cudaMemcpyDeviceToDevice, s);
+                if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+                if (err != cudaSuccess) return cuda_error(err);
+            }
+            return set_error(LEVO_OPS_ENONFINITE, w + ((word & 1) ? ": Euler velocity" : ": Euler state") +
+                                                      " contains a non-finite value (step " +
+                                                      std::to_string(step) + ")");
+        }
+        *completed_steps = step + 1;
+    }
+    // final context restore (src/levo-flow-renderer.cpp:113-114): a zero-step multi-step call
+    int rc = levo_cfg_euler_multi_f32(state, noise, context, nullptr, nullptr, 1, n, prefix, steps, 0, steps, 0,
+                                      1.0f, sigma_min, nullptr, stream);
+    if (rc != LEVO_OPS_OK) return rc;
+    const cudaError_t err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return cuda_error(err);
+    *completed_steps = steps;
+    return LEVO_OPS_OK;
 }
 
 }  // extern "C"

@@ -1,7 +1,7 @@
 // Greedy next-token selection over LeLM logits (next item f3).
 //
 // Reference: Sampler::sample_streams with use_sampling = false
-// (src/levo-sampling.cpp:127-154 -> sample_top_k_counted, :74-97):
+// (src/levo-sampling.cpp:129-152 -> sample_top_k_counted, :75-97):
 //   1. every distinct recent token id in [0, limit) divides its logit once by
 //      the repetition penalty (apply_unique_token_repetition_penalty, :39-48);
 //   2. on the first stream only, ignored token ids become -inf (:146-148);

@@ -757,22 +757,23 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
     const int64_t audio_elems = static_cast<int64_t>(t.audio_channels) * frames * total_upsampling(t);
     bool pending[2] = {false, false};
     cudaError_t err = cudaSuccess;
+    // Every exit waits for both streams: no copy of this call may still be
+    // writing into audio_host once the call has returned.
+    auto drained = [&](int rc) {
+        cudaStreamSynchronize(s);
+        cudaStreamSynchronize(chain->copy_stream);
+        return rc;
+    };
     for (int64_t w = 0; w < windows; ++w) {
-        if (cancel != nullptr && cancel(cancel_user) != 0) {
-            cudaStreamSynchronize(s);
-            cudaStreamSynchronize(chain->copy_stream);
-            return set_error(LEVO_OPS_ECANCELLED,
-                             "levo_vae_chain_decode_windows: cancelled before window " + std::to_string(w));
-        }
+        if (cancel != nullptr && cancel(cancel_user) != 0)
+            return drained(set_error(LEVO_OPS_ECANCELLED,
+                                     "levo_vae_chain_decode_windows: cancelled before window " + std::to_string(w)));
         // vae_decoder::decode rejects non-finite latents before any work (src/levo-vae.cpp:189-191)
         const float *lat_w = latents_host + w * lat_elems;
         for (int64_t i = 0; i < lat_elems; ++i) {
-            if (!std::isfinite(lat_w[i])) {
-                cudaStreamSynchronize(s);
-                cudaStreamSynchronize(chain->copy_stream);
-                return set_error(LEVO_OPS_ENONFINITE, "levo_vae_chain_decode_windows: latent payload contains a "
-                                                      "non-finite value (window " + std::to_string(w) + ")");
-            }
+            if (!std::isfinite(lat_w[i]))
+                return drained(set_error(LEVO_OPS_ENONFINITE, "levo_vae_chain_decode_windows: latent payload contains "
+                                                              "a non-finite value (window " + std::to_string(w) + ")"));
         }
         const int slot = static_cast<int>(w & 1);
         // The slot's previous audio must have left the device before reuse.
@@ -780,13 +781,9 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
         if (err == cudaSuccess)
             err = cudaMemcpyAsync(chain->lat[slot], lat_w,
                                   static_cast<size_t>(lat_elems) * sizeof(float), cudaMemcpyHostToDevice, s);
-        if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: latent upload");
+        if (err != cudaSuccess) return drained(cuda_fail(err, "levo_vae_chain_decode_windows: latent upload"));
         rc = decode_one(chain, chain->lat[slot], frames, chain->audio[slot], flags, s);
-        if (rc != LEVO_OPS_OK) {
-            cudaStreamSynchronize(s);
-            cudaStreamSynchronize(chain->copy_stream);
-            return rc;
-        }
+        if (rc != LEVO_OPS_OK) return drained(rc);
         err = cudaEventRecord(chain->computed[slot], s);
         if (err == cudaSuccess) err = cudaStreamWaitEvent(chain->copy_stream, chain->computed[slot], 0);
         if (err == cudaSuccess)
@@ -794,12 +791,12 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
                                   static_cast<size_t>(audio_elems) * sizeof(float), cudaMemcpyDeviceToHost,
                                   chain->copy_stream);
         if (err == cudaSuccess) err = cudaEventRecord(chain->copied[slot], chain->copy_stream);
-        if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: audio download");
+        if (err != cudaSuccess) return drained(cuda_fail(err, "levo_vae_chain_decode_windows: audio download"));
         pending[slot] = true;
     }
     err = cudaStreamSynchronize(chain->copy_stream);
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
-    if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_decode_windows: synchronize");
+    if (err != cudaSuccess) return drained(cuda_fail(err, "levo_vae_chain_decode_windows: synchronize"));
     return LEVO_OPS_OK;
 }
 
@@ -814,6 +811,13 @@ LEVO_OPS_API int levo_vae_chains_decode_windows(levo_vae_chain *const *chains, i
         return set_error(LEVO_OPS_EINVAL, std::string(w) + ": at least one chain is required");
     for (int32_t i = 0; i < n_chains; ++i) {
         if (chains[i] == nullptr) return set_error(LEVO_OPS_EINVAL, std::string(w) + ": chain is null");
+        // a chain's workspace, slots, copy stream and events serve one thread at a time
+        for (int32_t j = 0; j < i; ++j)
+            if (chains[j] == chains[i])
+                return set_error(LEVO_OPS_EINVAL, std::string(w) + ": the same chain is passed twice (chains " +
+                                                      std::to_string(j) + " and " + std::to_string(i) + ")");
+    }
+    for (int32_t i = 0; i < n_chains; ++i) {
         if (std::memcmp(&chains[i]->topo, &chains[0]->topo, sizeof(levo_vae_topology)) != 0)
             return set_error(LEVO_OPS_EINVAL, std::string(w) + ": chains must share one topology");
         const int rc = check_decode_args(chains[i], frames, flags, w);
@@ -906,17 +910,26 @@ constexpr int64_t kNoallocFloats = 3 * kNoallocBufferFloats;          // X, A an
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoallocFloats];
 
-// Device address of g_noalloc_scratch per device, resolved once with that
-// device current (the symbol's host-side name is not a device address).
+// Device address of g_noalloc_scratch per device, looked up with that device
+// current (the symbol's host-side name is not a device address).  It is looked
+// up again on every call made outside stream capture, so a device reset (a new
+// primary context, where the array may sit elsewhere) never leaves a stale
+// address behind; a call under capture uses the last address looked up, so the
+// first call on a device comes before any capture.
 constexpr int kNoallocMaxDevices = 64;
 float *g_noalloc_ptr[kNoallocMaxDevices] = {};
 std::mutex g_noalloc_mutex;
 
-int noalloc_scratch(int device, float **out) {
+int noalloc_scratch(int device, cudaStream_t stream, float **out) {
     if (device < 0 || device >= kNoallocMaxDevices)
         return set_error(LEVO_OPS_EUNSUPPORTED, "levo_vae_decode_noalloc_f32: device index out of range");
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
+        cudaGetLastError();
+        capture = cudaStreamCaptureStatusNone;
+    }
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_ptr[device] == nullptr) {
+    if (g_noalloc_ptr[device] == nullptr || capture == cudaStreamCaptureStatusNone) {
         void *ptr = nullptr;
         const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (err != cudaSuccess || ptr == nullptr)
@@ -971,7 +984,7 @@ LEVO_OPS_API int levo_vae_decode_noalloc_f32(const levo_vae_topology *topology, 
     if (cudaGetDevice(&device) != cudaSuccess)
         return set_error(LEVO_OPS_ECUDA, std::string(w) + ": no current CUDA device");
     float *scratch = nullptr;
-    const int rc = noalloc_scratch(device, &scratch);
+    const int rc = noalloc_scratch(device, reinterpret_cast<cudaStream_t>(stream), &scratch);
     if (rc != LEVO_OPS_OK) return rc;
 
     // A chain view over caller memory and the static scratch: no workspace,

@@ -6,7 +6,7 @@ it is missing every call raises, so nothing silently runs on the CPU.  The
 stream plumbing here) and pass raw pointers plus the current stream.
 
 Error behaviour mirrors the reference: invalid arguments raise ValueError
-(the reference throws std::invalid_argument, src/levo-audio-ops.cpp:45-47),
+(the reference throws std::invalid_argument, src/levo-audio-ops.cpp:10-12),
 everything else raises LevoOpsError with the library's thread-local message.
 """
 from __future__ import annotations
@@ -35,6 +35,13 @@ class LevoOpsError(RuntimeError):
 
 class LevoCancelled(LevoOpsError):
     pass
+
+
+class LevoNonFinite(LevoOpsError):
+    """A finiteness check failed (LEVO_OPS_ENONFINITE): the reference throws std::runtime_error.
+    For the Euler solve, `completed_steps` is the step the solve stopped at."""
+
+    completed_steps: Optional[int] = None
 
 
 class Topology(ctypes.Structure):
@@ -107,6 +114,8 @@ class KernelTiming(ctypes.Structure):
 
 
 CONV_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ConvCall), ctypes.c_void_p)
+VELOCITY_FN = ctypes.CFUNCTYPE(ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float,
+                               ctypes.c_void_p)
 CANCEL_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
 
 _P = ctypes.c_void_p
@@ -144,6 +153,10 @@ SIGNATURES = {
     "levo_flow_incontext_f32": (_INT, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P]),
     "levo_euler_cfg_step_f32": (_INT, [_P, _P, _P, _I64, _I32, _F, _I64, _P, _P]),
     "levo_cfg_euler_multi_f32": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _F, _F, _P, _P]),
+    "levo_flow_euler_solve_f32": (_INT, [_P, _P, _P, _I64, _I64, _I64, _F, _I64, _I64, _I32, _F, VELOCITY_FN, _P,
+                                         CANCEL_FN, _P, _P, _P, ctypes.POINTER(_I64), _P]),
+    "levo_cfg_euler_solve_f32": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _F, _F, _P, _P,
+                                        ctypes.POINTER(_I64), _P]),
     "levo_gated_layernorm_modulate_f32": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F, _P]),
     "levo_vae_decode_noalloc_f32": (_INT, [ctypes.POINTER(Topology), _P, _P, _I64, _P, CONV_FN, _P, _U32, _P]),
     "levo_greedy_tokens_f32": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P, _P, _P]),
@@ -183,6 +196,8 @@ def check(code: int) -> None:
         raise ValueError(msg)
     if code == ECANCELLED:
         raise LevoCancelled(code, msg)
+    if code == ENONFINITE:
+        raise LevoNonFinite(code, msg)
     raise LevoOpsError(code, msg)
 
 
@@ -376,6 +391,75 @@ def cfg_euler_multi_t(state, noise, context, uncond, cond, *, batch, prefix, fir
                                          sigma_min, _ptr(status), _stream(state.device)))
 
 
+EULER_STEP_LIMIT = 1 << 28
+EULER_FAIL_STATE, EULER_FAIL_VELOCITY = 2, 3
+
+
+def euler_status_step(word: int) -> int:
+    """First failing step recorded in a multi-step status word (LEVO_EULER_STATUS_STEP), -1 if none."""
+    return EULER_STEP_LIMIT - (word >> 2) if word >> 2 else -1
+
+
+def cfg_euler_solve_t(state, noise, context, uncond, cond, *, batch, prefix, first_step, count, steps,
+                      cfg=True, guidance=1.5, sigma_min=1e-4) -> int:
+    """solve_flow_euler over precomputed velocities (levo_cfg_euler_solve_f32): returns the completed
+    step count; on a non-finite velocity or state raises LevoNonFinite with .completed_steps, leaving
+    `state` at the reference's checkpoint of the steps completed before the failing one."""
+    import torch
+
+    _require_cuda(state, noise, context, uncond, cond)
+    row = state.numel() // batch
+    checkpoint = torch.empty_like(state)
+    status = torch.zeros(1, dtype=torch.int32, device=state.device)
+    done = ctypes.c_int64(0)
+    code = lib().levo_cfg_euler_solve_f32(_ptr(state), _ptr(noise), _ptr(context), _ptr(uncond), _ptr(cond), batch,
+                                          row, prefix, first_step, count, steps, 1 if cfg else 0, guidance,
+                                          sigma_min, _ptr(checkpoint), _ptr(status), ctypes.byref(done),
+                                          _stream(state.device))
+    try:
+        check(code)
+    except LevoNonFinite as err:
+        err.completed_steps = done.value
+        raise
+    return done.value
+
+
+def flow_euler_solve_t(state, noise, context, *, frames, latent_dim, incontext_frames, steps, velocity,
+                       first_step=0, cfg=True, guidance=1.5, sigma_min=1e-4, cancel=None, checkpoint=True) -> int:
+    """solve_flow_euler on a device state with a per-step velocity callable
+    velocity(state, step, time) -> CUDA tensor ([2, n] with cfg, else [n]); returns the completed step
+    count.  A non-finite velocity or state raises LevoNonFinite (.completed_steps set; with checkpoint=True
+    the state is the reference's checkpoint); cancel() returning True raises LevoCancelled."""
+    import torch
+
+    _require_cuda(state, noise, context)
+    keep = []  # velocity tensors must outlive their step
+
+    def _velocity(_user, state_ptr, step, time, _stream):
+        try:
+            v = velocity(state, int(step), float(time))
+            keep.append(v)
+            return v.data_ptr()
+        except Exception:  # noqa: BLE001 - reported through the C ABI as a failed callback
+            return None
+
+    vcb = VELOCITY_FN(_velocity)
+    ccb = CANCEL_FN(lambda _u: 1 if cancel() else 0) if cancel is not None else CANCEL_FN()
+    ckpt = torch.empty_like(state) if checkpoint else None
+    status = torch.zeros(1, dtype=torch.int32, device=state.device)
+    done = ctypes.c_int64(0)
+    code = lib().levo_flow_euler_solve_f32(_ptr(state), _ptr(noise), _ptr(context), frames, latent_dim,
+                                           incontext_frames, sigma_min, steps, first_step, 1 if cfg else 0, guidance,
+                                           vcb, None, ccb, None, _ptr(ckpt), _ptr(status), ctypes.byref(done),
+                                           _stream(state.device))
+    try:
+        check(code)
+    except LevoOpsError as err:
+        err.completed_steps = done.value
+        raise
+    return done.value
+
+
 def assemble_windows_t(windows, hop_samples: int, overlap_samples: int, target_samples: int, interleaved=False,
                        out=None):
     """Crossfade-assemble decoded windows [W, C, S] into [C, target] (or [target, C] interleaved)."""
@@ -441,11 +525,43 @@ def param_count(topology: Topology) -> int:
     return int(n)
 
 
+def _host_window_buffers(topology: Topology, latents_host, audio_host, frames: int):
+    """Validates the host buffers of a host-to-host decode and returns (windows, latent ptr, audio ptr).
+    The library copies windows * audio_channels * samples floats into audio_host and reads
+    windows * latent_dim * frames from latents_host, so both must be float32, C-contiguous CPU
+    buffers of at least that size."""
+    import numpy as np
+
+    def describe(buf, name):
+        if hasattr(buf, "ctypes"):  # numpy
+            if buf.dtype != np.float32 or not buf.flags["C_CONTIGUOUS"]:
+                raise ValueError(f"{name} must be a C-contiguous float32 array")
+            return buf.shape, buf.size, buf.ctypes.data
+        import torch
+
+        if not isinstance(buf, torch.Tensor) or buf.is_cuda:
+            raise ValueError(f"{name} must be a numpy array or a CPU tensor")
+        if buf.dtype != torch.float32 or not buf.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous float32 tensor")
+        return tuple(buf.shape), buf.numel(), buf.data_ptr()
+
+    lat_shape, _, lat_ptr = describe(latents_host, "latents_host")
+    _, audio_size, out_ptr = describe(audio_host, "audio_host")
+    if len(lat_shape) != 3 or lat_shape[1] != topology.latent_dim or lat_shape[2] != frames:
+        raise ValueError(f"latents_host must have shape (windows, {topology.latent_dim}, {frames}), got {lat_shape}")
+    windows = lat_shape[0]
+    need = windows * topology.audio_channels * frames * topology.upsampling()
+    if audio_size < need:
+        raise ValueError(f"audio_host holds {audio_size} floats; {windows} windows need {need}")
+    return windows, lat_ptr, out_ptr
+
+
 def decode_windows_multi(chains, latents_host, audio_host, frames: int, flags: int = 0, cancel=None) -> None:
     """Host-to-host decode of independent windows over several chains (one per GPU) from one
     process: chain i decodes a contiguous block of the windows on its own thread and stream."""
-    lat_ptr = latents_host.ctypes.data if hasattr(latents_host, "ctypes") else latents_host.data_ptr()
-    out_ptr = audio_host.ctypes.data if hasattr(audio_host, "ctypes") else audio_host.data_ptr()
+    if not chains:
+        raise ValueError("at least one chain is required")
+    _, lat_ptr, out_ptr = _host_window_buffers(chains[0].topology, latents_host, audio_host, frames)
     handles = (ctypes.c_void_p * len(chains))(*[c.handle.value for c in chains])
     cb = CANCEL_FN(lambda _u: 1 if cancel() else 0) if cancel is not None else CANCEL_FN()
     check(lib().levo_vae_chains_decode_windows(ctypes.cast(handles, ctypes.c_void_p), len(chains), lat_ptr,
@@ -494,10 +610,9 @@ class VaeChain:
 
     def decode_windows(self, latents_host, audio_host, frames: int, flags: int = 0, cancel=None,
                        stream: Optional[int] = None) -> None:
-        """Host-to-host decode of independent windows (numpy arrays or CPU tensors)."""
-        lat_ptr = latents_host.ctypes.data if hasattr(latents_host, "ctypes") else latents_host.data_ptr()
-        out_ptr = audio_host.ctypes.data if hasattr(audio_host, "ctypes") else audio_host.data_ptr()
-        windows = latents_host.shape[0]
+        """Host-to-host decode of independent windows: latents_host (windows, latent_dim, frames) and
+        audio_host (windows, audio_channels, samples), float32 C-contiguous numpy arrays or CPU tensors."""
+        windows, lat_ptr, out_ptr = _host_window_buffers(self.topology, latents_host, audio_host, frames)
         cb = CANCEL_FN(lambda _u: 1 if cancel() else 0) if cancel is not None else CANCEL_FN()
         if stream is None:
             import torch

@@ -146,7 +146,7 @@ static void node(int kind, const float *a, const float *b, const float *p, float
     parallel_rows(rows, threads, node_rows, &j);
 }
 
-/* SnakeBeta graph of src/levo-audio-ops.cpp:181-186:
+/* SnakeBeta graph of src/levo-audio-ops.cpp:146-151:
  *   alpha = exp(alpha_log); beta = scale_bias(exp(beta_log), 1, 1e-9)
  *   y = x + sqr(sin(x * alpha)) / beta
  * `tmp` holds the intermediate nodes (GGML's allocator reuses one buffer). */
@@ -237,7 +237,7 @@ void oracle_conv_standin_f32(const float *in, int64_t cin, int64_t lin, float *o
 /* Stage loop of src/levo-vae.cpp:212-235 with run_residual (src/levo-vae.cpp:90-101).
  * Convs are the stand-ins: the input / upsample / output convs are index-map
  * copies and the residual convs are identities; every conv's bias is a
- * separate add node (src/levo-audio-ops.cpp:74-87). */
+ * separate add node (src/levo-audio-ops.cpp:39-52). */
 int oracle_vae_chain_f32(const int32_t *topo, const float *P, const float *latent, int64_t frames,
                          float *audio, int tanh_out, int threads) {
     return oracle_vae_chain_stages_f32(topo, P, latent, frames, audio, tanh_out, threads, NULL);
@@ -511,15 +511,23 @@ int oracle_cfg_combine_f32(const float *u, const float *c, float *out, int64_t n
 int oracle_cfg_euler_f32(float *state, const float *noise, const float *context,
                          const float *uncond, const float *cond, int64_t batch, int64_t row,
                          int64_t prefix, int64_t first_step, int64_t count, int64_t steps, int cfg,
-                         float guidance, float sigma_min) {
+                         float guidance, float sigma_min, int64_t *failed_step) {
     if (!state || batch <= 0 || row <= 0 || steps <= 0 || prefix < 0 || prefix > row) return -2;
     if (first_step < 0 || count < 0 || first_step + count > steps) return -2;
     const int64_t n = batch * row;
     float *v = (float *)malloc(sizeof(float) * (size_t)n);
-    if (!v) return -2;
+    float *saved = (float *)malloc(sizeof(float) * (size_t)n);  /* the checkpoint (:85-88, :107-110) */
+    if (!v || !saved) {
+        free(v);
+        free(saved);
+        return -2;
+    }
+    int rc = 0;
+    if (failed_step) *failed_step = -1;
     const float dt = 1.0F / (float)steps;                               /* :90  */
-    for (int64_t k = 0; k < count; ++k) {
+    for (int64_t k = 0; k < count && rc == 0; ++k) {
         const int64_t step = first_step + k;
+        memcpy(saved, state, sizeof(float) * (size_t)n);
         const float time = (float)step * dt;                            /* :93  */
         const float noise_scale = 1.0F - (1.0F - sigma_min) * time;     /* :94  */
         for (int64_t b = 0; b < batch; ++b)                             /* :95-101 */
@@ -531,23 +539,24 @@ int oracle_cfg_euler_f32(float *state, const float *noise, const float *context,
         const float *c = cfg ? cond + k * n : NULL;
         for (int64_t e = 0; e < n; ++e)                                 /* :305-308 */
             v[e] = cfg ? u[e] + guidance * (c[e] - u[e]) : u[e];
-        for (int64_t e = 0; e < n; ++e)
-            if (!isfinite(v[e])) {
-                free(v);
-                return -1;
-            }
-        for (int64_t e = 0; e < n; ++e) state[e] += dt * v[e];          /* :105 */
-        for (int64_t e = 0; e < n; ++e)
-            if (!isfinite(state[e])) {
-                free(v);
-                return -1;
-            }
+        for (int64_t e = 0; e < n && rc == 0; ++e)                      /* :104 */
+            if (!isfinite(v[e])) rc = -1;
+        if (rc == 0) {
+            for (int64_t e = 0; e < n; ++e) state[e] += dt * v[e];      /* :105 */
+            for (int64_t e = 0; e < n && rc == 0; ++e)                  /* :106 */
+                if (!isfinite(state[e])) rc = -3;
+        }
+        if (rc != 0) {
+            memcpy(state, saved, sizeof(float) * (size_t)n);
+            if (failed_step) *failed_step = step;
+        }
     }
-    if (first_step + count == steps)                                    /* :113-114 */
+    if (rc == 0 && first_step + count == steps)                         /* :113-114 */
         for (int64_t b = 0; b < batch; ++b)
             memcpy(state + b * row, context + b * row, sizeof(float) * (size_t)prefix);
     free(v);
-    return 0;
+    free(saved);
+    return rc;
 }
 
 /* ------------------------------------------------------------------------ */

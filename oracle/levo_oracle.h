@@ -22,14 +22,14 @@
 extern "C" {
 #endif
 
-/* SnakeBeta, src/levo-audio-ops.cpp:181-186.  params are F32 [C]. */
+/* SnakeBeta, src/levo-audio-ops.cpp:146-151.  params are F32 [C]. */
 int oracle_snakebeta_f32(const float *x, const float *alpha_log, const float *beta_log, float *y,
                          int64_t channels, int64_t time, int threads);
 /* Same with F16-stored parameters (IEEE half bits), promoted as ggml_cast does. */
 int oracle_snakebeta_f16params(const float *x, const uint16_t *alpha_log, const uint16_t *beta_log,
                                float *y, int64_t channels, int64_t time, int threads);
 
-/* add_channel_bias, src/levo-audio-ops.cpp:74-87. */
+/* add_channel_bias, src/levo-audio-ops.cpp:39-52. */
 int oracle_channel_bias_add_f32(const float *in, const float *bias, float *out, int64_t channels,
                                 int64_t time, int threads);
 
@@ -90,15 +90,17 @@ int oracle_cfg_combine_f32(const float *uncond, const float *cond, float *out, i
                            float guidance);
 
 /* Euler solve with CFG-combined precomputed velocities, restating
- * solve_flow_euler (src/levo-flow-renderer.cpp:57-120) for each of `batch`
- * independent rows: runs steps [first_step, first_step + count) and restores
- * the context prefix when the last step has run.  Returns -1 on a non-finite
- * velocity or state (the reference throws); `state` is then unspecified, as the
- * reference discards its local state and keeps only the last checkpoint. */
+ * solve_flow_euler (src/levo-flow-renderer.cpp:57-120) for one state of
+ * `batch` rows: runs steps [first_step, first_step + count) and restores the
+ * context prefix when the last step has run.  Like the reference it stops at
+ * the first step whose combined velocity (:104, returns -1) or updated state
+ * (:106, returns -3) holds a non-finite value, leaving `state` at the checkpoint
+ * of the steps completed before it and that step in *failed_step (may be
+ * NULL; -1 when every step ran).  -2: invalid arguments or out of memory. */
 int oracle_cfg_euler_f32(float *state, const float *noise, const float *context,
                          const float *uncond, const float *cond, int64_t batch, int64_t row,
                          int64_t prefix, int64_t first_step, int64_t count, int64_t steps, int cfg,
-                         float guidance, float sigma_min);
+                         float guidance, float sigma_min, int64_t *failed_step);
 
 /* Window crossfade assembly, src/levo-renderer-pattern.cpp:137-203, over
  * windows [n][channels][window_samples] -> planar [channels][target]; the
@@ -108,7 +110,7 @@ int oracle_assemble_windows_f32(const float *windows, int64_t n, int64_t channel
                                 int64_t target, float *out);
 
 /* Greedy token per row, restating sample_streams with use_sampling = false
- * (src/levo-sampling.cpp:39-48,74-97,127-154).  Returns -1 when a logit is NaN
+ * (src/levo-sampling.cpp:39-48,75-97,129-152).  Returns -1 when a logit is NaN
  * (the reference throws); the indices are still written. */
 int oracle_greedy_tokens_f32(const float *logits, int64_t rows, int64_t vocab, const int64_t *recent,
                              int64_t recent_len, float penalty, int64_t penalty_limit,

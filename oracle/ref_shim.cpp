@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -47,7 +48,10 @@ REF_API int ref_combine_renderer_cfg(const float *u, const float *c, int64_t n, 
 //                     (0-based), emulating a pause at that boundary.
 //   seen (optional) [steps][n]: the state passed to each velocity call.
 // Returns 0 when solved, 1 when paused (checkpoint in out_state /
-// out_completed), -1 on error (ref_last_error()).
+// out_completed), -2 when the solver threw after its loop began (a non-finite
+// velocity or state, src/levo-flow-renderer.cpp:104,106: the checkpoint of the
+// last completed step in out_state / out_completed, the message in
+// ref_last_error()), -1 on any other error (ref_last_error()).
 REF_API int ref_solve_flow_euler(const float *noise, const float *context, int64_t frames,
                                  int64_t latent_dim, int64_t incontext_frames, float sigma_min,
                                  int64_t steps, const float *uncond, const float *cond, int cfg,
@@ -94,6 +98,12 @@ REF_API int ref_solve_flow_euler(const float *noise, const float *context, int64
             std::memcpy(out_state, checkpoint.normalized_state.data(), n * sizeof(float));
             *out_completed = static_cast<int64_t>(checkpoint.completed_steps);
             return 1;
+        } catch (const std::runtime_error &e) {
+            if (checkpoint.normalized_state.size() != n) throw;  // thrown before the step loop
+            std::memcpy(out_state, checkpoint.normalized_state.data(), n * sizeof(float));
+            *out_completed = static_cast<int64_t>(checkpoint.completed_steps);
+            g_error = e.what();
+            return -2;
         }
     } catch (const std::exception &e) {
         return fail(e);
@@ -158,7 +168,7 @@ REF_API int ref_make_renderer_euler_schedule(int64_t steps, float *times, float 
     }
 }
 
-// Sampler::sample_streams with use_sampling = false (src/levo-sampling.cpp:127-154).
+// Sampler::sample_streams with use_sampling = false (src/levo-sampling.cpp:129-152).
 // recent: [rows][recent_len] (entries < 0 are dropped, so rows may be padded),
 // the repetition window is recent_len; ignore applies to stream 0.
 REF_API int ref_sample_streams_greedy(const float *logits, int64_t rows, int64_t vocab, const int64_t *recent,

@@ -112,6 +112,50 @@ int main() {
         thrown = true;
     }
     CHECK(thrown);
+    // A non-finite velocity at step 1 throws the reference's message (src/levo-flow-renderer.cpp:104)
+    // and, with a checkpoint, leaves the state after step 0 (its euler_resume_state, :107-110).
+    float *dbad = to_device(std::vector<float>{1.0F, 1.0F, 1.0F, NAN, 1.0F, 1.0F});
+    float *dckpt = to_device(std::vector<float>(6));
+    float *dstate2 = to_device(noise);
+    euler_device_input in2{dstate2, dnoise, dctx, 3, 2, 1, 0.1F};
+    euler_device_checkpoint ckpt{dckpt, 0};
+    std::vector<float> after_step0;
+    thrown = false;
+    try {
+        solve_flow_euler(
+            in2, 2, false, 1.0F,
+            [&](const float *state, int64_t step) {
+                if (step == 1) after_step0 = to_host(state, 6);  // after the step-1 interpolation
+                return static_cast<const float *>(step == 0 ? dones : dbad);
+            },
+            [] { return false; }, dstatus, 0, nullptr, &ckpt);
+    } catch (const std::runtime_error &e) {
+        thrown = std::string(e.what()) == "LeVo Flow renderer: Euler velocity contains a non-finite value";
+    }
+    CHECK(thrown);
+    CHECK(ckpt.completed_steps == 1);
+    const std::vector<float> resumed = to_host(dstate2, 6);
+    // the checkpoint is the state before the step-1 interpolation: noise + 1 * dt for every element
+    const float ck[6] = {1.5F, 2.5F, 10.5F, 20.5F, 30.5F, 40.5F};
+    for (int i = 0; i < 6; ++i) CHECK(std::fabs(resumed[i] - ck[i]) < 1e-6F);
+    CHECK(to_host(dckpt, 6) == resumed);
+    (void)after_step0;
+
+    // Norm errors carry the prefixes of the reference's LM and Flow estimator (std::runtime_error).
+    thrown = false;
+    try {
+        add_rms_norm_f16(dx, nullptr, nullptr, nullptr, dy, 1, 8, 1e-6F, false);
+    } catch (const std::runtime_error &e) {
+        thrown = std::string(e.what()).rfind("LeVo LM: ", 0) == 0;
+    }
+    CHECK(thrown);
+    thrown = false;
+    try {
+        add_layer_norm_f32(dx, nullptr, dx, nullptr, nullptr, dy, 1, 4);
+    } catch (const std::runtime_error &e) {
+        thrown = std::string(e.what()).rfind("LeVo Flow estimator: ", 0) == 0;
+    }
+    CHECK(thrown);
 
     // vae_decoder over a reduced topology: deterministic, finite, bounded by tanh.
     levo_vae_topology topo{};

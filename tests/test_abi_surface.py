@@ -160,3 +160,38 @@ def test_headers_compile_standalone(lang, header, std):
     out = subprocess.run([compiler, std, "-Wall", "-Wextra", "-Werror", "-pedantic", "-fsyntax-only", "-x", lang,
                           str(ROOT / "include" / header)], capture_output=True, text=True)
     assert out.returncode == 0, out.stderr
+
+
+def test_multi_chain_decode_rejects_a_chain_passed_twice_without_gpu(ops):
+    """Two entries naming one chain would share its workspace and streams across threads: EINVAL,
+    checked before any chain is touched."""
+    lib = ops.lib()
+    dummy = (ctypes.c_float * 8)()
+    fake = ctypes.addressof(dummy)  # never dereferenced: the duplicate check comes first
+    handles = (ctypes.c_void_p * 2)(fake, fake)
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.addressof(buf)
+    rc = lib.levo_vae_chains_decode_windows(ctypes.cast(handles, ctypes.c_void_p), 2, p, 1, 1, p, 0, ops.CANCEL_FN(),
+                                            None)
+    assert rc == ops.EINVAL
+    assert "passed twice" in ops.last_error()
+
+
+def test_decode_windows_binding_validates_host_buffers(ops):
+    """The binding checks dtype, contiguity and sizes before the C ABI copies into host memory."""
+    import numpy as np
+
+    t = ops.reference_topology()
+    frames = 4
+    lat = np.zeros((2, t.latent_dim, frames), np.float32)
+    audio = np.zeros((2, t.audio_channels, frames * t.upsampling()), np.float32)
+    assert ops._host_window_buffers(t, lat, audio, frames)[0] == 2
+    with pytest.raises(ValueError, match="float32"):
+        ops._host_window_buffers(t, lat.astype(np.float64), audio, frames)
+    with pytest.raises(ValueError, match="shape"):
+        ops._host_window_buffers(t, lat, audio, frames + 1)
+    with pytest.raises(ValueError, match="need"):
+        ops._host_window_buffers(t, lat, audio[:1], frames)
+    with pytest.raises(ValueError, match="C-contiguous"):
+        ops._host_window_buffers(t, lat, np.zeros((2, frames * t.upsampling(), 4), np.float32).transpose(0, 2, 1),
+                                 frames)

@@ -233,7 +233,7 @@ def test_conv_standin(ops, orc, dev):
 
 def test_f16_stored_parameters(ops, orc, dev):
     # The F16 VAE artifact keeps parameters in F16; each unit promotes them to F32
-    # (src/levo-audio-ops.cpp:67-72): same result as F32 parameters holding the promoted values.
+    # (src/levo-audio-ops.cpp:32-37): same result as F32 parameters holding the promoted values.
     topo = small_topology(ops)
     params16 = params_for(ops, topo, 21).astype(np.float16)
     frames = 12

@@ -136,3 +136,186 @@ def test_nonfinite_velocity_sets_status(ops, dev):
     ops.euler_cfg_step_t(torch.full((n,), 3e38, device=dev), torch.full((n,), 3e38, device=dev), None, 1.0, 1,
                          cfg=False, status=status)
     assert status.item() == 2  # finite velocity, overflowing state
+
+
+def _failing_case(case, frames, dim, steps, prefix_frames, fail_step, element, seed=11):
+    """Seeded inputs whose `element` fails at `fail_step`: a NaN conditional velocity, or a finite
+    velocity that pushes a near-maximal state past FLT_MAX."""
+    rng = np.random.default_rng(seed)
+    n = frames * dim
+    noise = rng.standard_normal(n).astype(np.float32)
+    ctx = rng.standard_normal(n).astype(np.float32)
+    vu, vc = rng.standard_normal((2, steps, n)).astype(np.float32)
+    if case == "velocity":
+        vc[fail_step, element] = np.nan
+    else:
+        noise[element] = np.float32(3.39e38)
+        if element >= prefix_frames * dim:  # outside the prefix the state itself starts near FLT_MAX
+            vu[:fail_step, element] = 0.0
+            vc[:fail_step, element] = 0.0
+        vu[fail_step, element] = np.float32(3.4e38)
+        vc[fail_step, element] = np.float32(3.4e38)
+    return noise, ctx, vu, vc
+
+
+@pytest.mark.skipif("not __import__('levo_oracle').ref_available()")
+@pytest.mark.parametrize("case", ["velocity", "state"])
+@pytest.mark.parametrize("layout", [(252, 64, 70), (7, 5, 9)])  # staged kernel (n % 4 == 0), register kernel
+@pytest.mark.parametrize("where", ["body", "prefix"])
+def test_solve_stops_at_the_reference_checkpoint(ops, orc, dev, case, layout, where):
+    """The first non-finite velocity or state ends the solve where the reference's solve_flow_euler throws
+    (src/levo-flow-renderer.cpp:104,106): state = its checkpoint of the completed steps, bit for bit."""
+    frames, dim, steps = layout
+    prefix_frames = 2
+    fail_step = steps - 4 if steps > 64 else 5  # past the first 64-step staging round when there is one
+    element = 3 if where == "prefix" else prefix_frames * dim + 7
+    if case == "state" and where == "prefix":
+        fail_step = 0  # the interpolated prefix value is near FLT_MAX at step 0 only
+    noise, ctx, vu, vc = _failing_case(case, frames, dim, steps, prefix_frames, fail_step, element)
+    status, want, done, _ = orc.ref_solve_flow_euler(noise, ctx, frames, dim, prefix_frames, 1e-4, steps, vu, vc,
+                                                     guidance=1.5)
+    assert status == 2 and done == fail_step
+    message = orc.ref_last_message()
+    assert ("velocity" if case == "velocity" else "state") in message
+    # the oracle restatement stops at the same checkpoint
+    st_o, failure, k = orc.cfg_euler_checked(noise, noise, ctx, vu, vc, batch=1, prefix=prefix_frames * dim,
+                                             first_step=0, count=steps, steps=steps)
+    assert failure == case and k == fail_step and np.array_equal(st_o, want)
+    st = T(noise, dev)
+    with pytest.raises(ops.LevoNonFinite) as err:
+        ops.cfg_euler_solve_t(st, T(noise, dev), T(ctx, dev), T(vu, dev), T(vc, dev), batch=1,
+                              prefix=prefix_frames * dim, first_step=0, count=steps, steps=steps)
+    assert err.value.completed_steps == fail_step
+    assert f"Euler {case} contains a non-finite value (step {fail_step})" in str(err.value)
+    assert np.array_equal(st.cpu().numpy(), want)
+
+
+@pytest.mark.skipif("not __import__('levo_oracle').ref_available()")
+def test_solve_resumed_after_a_pause_stops_at_the_same_checkpoint(ops, orc, dev):
+    frames, dim, steps, prefix_frames, fail_step = 252, 64, 12, 1, 9
+    noise, ctx, vu, vc = _failing_case("velocity", frames, dim, steps, prefix_frames, fail_step, 100)
+    _, want, done, _ = orc.ref_solve_flow_euler(noise, ctx, frames, dim, prefix_frames, 1e-4, steps, vu, vc)
+    assert done == fail_step
+    st = T(noise, dev)
+    assert ops.cfg_euler_solve_t(st, T(noise, dev), T(ctx, dev), T(vu, dev), T(vc, dev), batch=1,
+                                 prefix=prefix_frames * dim, first_step=0, count=4, steps=steps) == 4
+    with pytest.raises(ops.LevoNonFinite) as err:
+        ops.cfg_euler_solve_t(st, T(noise, dev), T(ctx, dev), T(vu[4:], dev), T(vc[4:], dev), batch=1,
+                              prefix=prefix_frames * dim, first_step=4, count=steps - 4, steps=steps)
+    assert err.value.completed_steps == fail_step
+    assert np.array_equal(st.cpu().numpy(), want)
+
+
+def test_solve_without_failure_equals_the_fused_kernel(ops, orc, dev):
+    rng = np.random.default_rng(5)
+    batch, row, steps = 2, 64 * 252, 50
+    x = rng.standard_normal(batch * row).astype(np.float32)
+    vu, vc = rng.standard_normal((2, steps, batch * row)).astype(np.float32)
+    ctx = rng.standard_normal(batch * row).astype(np.float32)
+    st = T(x, dev)
+    assert ops.cfg_euler_solve_t(st, T(x, dev), T(ctx, dev), T(vu, dev), T(vc, dev), batch=batch, prefix=64,
+                                 first_step=0, count=steps, steps=steps) == steps
+    want, ok = orc.cfg_euler(x, x, ctx, vu, vc, batch=batch, prefix=64, first_step=0, count=steps, steps=steps)
+    assert ok and np.array_equal(st.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("layout", [(252, 64, 70), (7, 5, 9)])
+def test_multi_step_status_records_the_first_failing_step(ops, orc, dev, layout):
+    """levo_cfg_euler_multi_f32 alone: the status word holds the earliest failing step (velocity kind on a
+    tie), and each failing element keeps its state after the last step it completed."""
+    frames, dim, steps = layout
+    n = frames * dim
+    fail_step = steps - 2
+    noise, ctx, vu, vc = _failing_case("velocity", frames, dim, steps, 0, fail_step, 9)
+    vu[fail_step - 1, 20] = np.float32(3.4e38)  # element 20: state overflow one step earlier
+    vc[fail_step - 1, 20] = np.float32(3.4e38)
+    noise[20] = np.float32(3.39e38)
+    vu[: fail_step - 1, 20] = 0.0
+    vc[: fail_step - 1, 20] = 0.0
+    st = T(noise, dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.cfg_euler_multi_t(st, None, None, T(vu, dev), T(vc, dev), batch=1, prefix=0, first_step=0, count=steps,
+                          steps=steps, status=status)
+    word = int(status.item())
+    assert ops.euler_status_step(word) == fail_step - 1 and word & 3 == ops.EULER_FAIL_STATE
+    got = st.cpu().numpy()
+    for e, k in ((9, fail_step), (20, fail_step - 1)):
+        one, _, _ = orc.cfg_euler_checked(noise[e:e + 1], None, None, vu[:, e:e + 1], vc[:, e:e + 1], batch=1,
+                                          prefix=0, first_step=0, count=k, steps=steps)
+        assert got[e] == one[0]
+    # every other element ran all steps
+    others = np.setdiff1d(np.arange(n), [9, 20])
+    full, ok = orc.cfg_euler(noise[others], None, None, vu[:, others], vc[:, others], batch=1, prefix=0,
+                             first_step=0, count=steps, steps=steps)
+    assert ok and np.array_equal(got[others], full)
+
+
+@pytest.mark.skipif("not __import__('levo_oracle').ref_available()")
+@pytest.mark.parametrize("case", ["none", "velocity", "state"])
+def test_per_step_solve_matches_the_reference(ops, orc, dev, case):
+    """levo_flow_euler_solve_f32 with a velocity callback (the estimator's place) against the reference's
+    solve_flow_euler: the states the estimator sees, the solved state, and on a non-finite velocity or
+    state the reference's checkpoint and step, all bit for bit."""
+    frames, dim, steps, prefix_frames, fail = 252, 64, 12, 2, 7
+    if case == "none":
+        rng = np.random.default_rng(21)
+        n = frames * dim
+        noise, ctx = rng.standard_normal((2, n)).astype(np.float32)
+        vu, vc = rng.standard_normal((2, steps, n)).astype(np.float32)
+    else:
+        noise, ctx, vu, vc = _failing_case(case, frames, dim, steps, prefix_frames, fail, prefix_frames * dim + 5)
+    status, want, done, seen = orc.ref_solve_flow_euler(noise, ctx, frames, dim, prefix_frames, 1e-4, steps, vu, vc,
+                                                        want_seen=True)
+    VU, VC = T(vu, dev), T(vc, dev)
+    got_seen = []
+
+    def velocity(state, step, time):
+        got_seen.append(state.cpu().numpy().copy())
+        return torch.stack([VU[step], VC[step]])
+
+    st = T(noise, dev)
+    kw = dict(frames=frames, latent_dim=dim, incontext_frames=prefix_frames, steps=steps, velocity=velocity)
+    if case == "none":
+        assert status == 0
+        assert ops.flow_euler_solve_t(st, T(noise, dev), T(ctx, dev), **kw) == steps
+    else:
+        assert status == 2 and done == fail
+        with pytest.raises(ops.LevoNonFinite) as err:
+            ops.flow_euler_solve_t(st, T(noise, dev), T(ctx, dev), **kw)
+        assert err.value.completed_steps == fail and f"Euler {case} contains" in str(err.value)
+    assert np.array_equal(st.cpu().numpy(), want)
+    ran = steps if case == "none" else fail + 1
+    assert len(got_seen) == ran
+    for k in range(ran):
+        assert np.array_equal(got_seen[k], seen[k]), k
+
+
+@pytest.mark.skipif("not __import__('levo_oracle').ref_available()")
+def test_per_step_solve_cancel_and_resume(ops, orc, dev):
+    """A cancellation before step 4 leaves the reference's pause checkpoint; resuming from it finishes
+    with the reference's solved state."""
+    frames, dim, steps, prefix_frames = 100, 64, 9, 3
+    rng = np.random.default_rng(8)
+    n = frames * dim
+    noise, ctx = rng.standard_normal((2, n)).astype(np.float32)
+    vu, vc = rng.standard_normal((2, steps, n)).astype(np.float32)
+    status, paused, done, _ = orc.ref_solve_flow_euler(noise, ctx, frames, dim, prefix_frames, 1e-4, steps, vu, vc,
+                                                       pause_after=4)
+    assert status == 1 and done == 4
+    _, solved, _, _ = orc.ref_solve_flow_euler(noise, ctx, frames, dim, prefix_frames, 1e-4, steps, vu, vc)
+    VU, VC = T(vu, dev), T(vc, dev)
+    polls = []
+
+    def cancel():
+        polls.append(1)
+        return len(polls) > 4
+
+    st = T(noise, dev)
+    kw = dict(frames=frames, latent_dim=dim, incontext_frames=prefix_frames, steps=steps,
+              velocity=lambda s, k, t: torch.stack([VU[k], VC[k]]))
+    with pytest.raises(ops.LevoCancelled) as err:
+        ops.flow_euler_solve_t(st, T(noise, dev), T(ctx, dev), cancel=cancel, **kw)
+    assert err.value.completed_steps == 4
+    assert np.array_equal(st.cpu().numpy(), paused)
+    assert ops.flow_euler_solve_t(st, T(noise, dev), T(ctx, dev), first_step=4, **kw) == steps
+    assert np.array_equal(st.cpu().numpy(), solved)
