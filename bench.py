@@ -15,8 +15,8 @@ Extra keys of the JSON line:
                region) against the measured HBM copy bandwidth
   kernels      SnakeBeta (config 0), add+RMSNorm / add+LayerNorm / weight norm
                (config 1) and the fused 50-step CFG+Euler (config 2) in GB/s: per-launch
-               time of back-to-back launches over input sets larger than L2 in total
-               (rank 0, N = 1 only)
+               time of back-to-back launches (replayed from a CUDA graph) over input sets
+               larger than L2 in total (rank 0, N = 1 only)
   cpu_baseline the CPU oracle (node-by-node restatement, all host threads) on one whole
                window of the same frame count (rank 0, N = 1 only)
 
@@ -333,10 +333,12 @@ def input_sets(set_bytes: int) -> int:
 
 
 def kernel_suite(ops, dev, peak, steps, warmup):
-    """Configs 0-2 kernels.  `ms` is the per-launch time of KERNEL_LAUNCHES back-to-back launches
-    between one pair of CUDA events, rotating over input sets larger than L2 in total (median of
-    `steps` repetitions); `ms_single_launch` is one launch after an L2 flush, bracketed by its own
-    events, which also counts the launch latency and sits on the event timer's 2 us tick."""
+    """Configs 0-2 kernels.  `ms` is the per-launch time of KERNEL_LAUNCHES back-to-back launches,
+    rotating over input sets larger than L2 in total, captured once into a CUDA graph and replayed
+    between one pair of CUDA events (median of `steps` replays): device time, without the host
+    cost of each Python-side launch.  `ms_single_launch` is one eager launch after an L2 flush,
+    bracketed by its own events, which also counts the launch latency and sits on the event
+    timer's 2 us tick."""
     import torch
 
     rng = np.random.default_rng(SEED)
@@ -344,18 +346,25 @@ def kernel_suite(ops, dev, peak, steps, warmup):
     stream = torch.cuda.current_stream(dev)
 
     def timeit_rotating(fns):
-        for i in range(max(warmup, 1) * len(fns)):
+        for i in range(max(warmup, 1) * len(fns)):  # eager warm-up: every launch path resolved
             fns[i % len(fns)]()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(KERNEL_LAUNCHES):
+                fns[i % len(fns)]()
+        for _ in range(max(warmup, 1)):
+            graph.replay()
         per_launch = []
         for _ in range(steps):
             torch.cuda.synchronize(dev)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            for i in range(KERNEL_LAUNCHES):
-                fns[i % len(fns)]()
+            graph.replay()
             e1.record(stream)
             torch.cuda.synchronize(dev)
             per_launch.append(e0.elapsed_time(e1) / KERNEL_LAUNCHES)
+        del graph
         return statistics.median(per_launch)
 
     def timeit_single(fn):
@@ -455,6 +464,9 @@ def own_arm(args):
     torch.cuda.set_device(dev)
     pkg = entry.load_package()
     ops, sharding = pkg.ops, pkg.sharding
+    # One rank per GPU: run next to its GPU, so its pinned host buffers sit on that GPU's memory node
+    # (N = 1 keeps every host core for the CPU baseline).
+    local_cpus = sharding.bind_to_gpu_local_cpus(d.local) if d.world > 1 else None
     topo = ops.reference_topology()
     topo_l = topology_list(topo)
     params = make_params(topo_l)
@@ -511,7 +523,7 @@ def own_arm(args):
     lat_host = torch.from_numpy(latents[start:stop].copy()).pin_memory()
     gather = sharding.HostGather(sharding.run_tag() + "_bench", (args.windows, topo.audio_channels, samples), d.rank,
                                  d.barrier)
-    pinned = gather.pin()
+    pinned = gather.pin(start, stop)
     out_view = gather.view(start, stop)
 
     def e2e_step():
@@ -565,6 +577,7 @@ def own_arm(args):
                     "h2d_bytes_per_step": int(latents.nbytes),
                     "d2h_bytes_per_step": int(args.windows * topo.audio_channels * samples * 4),
                     "ms_per_step": e2e_ms, "host_buffers": "pinned" if pinned else "pageable",
+                    "host_cpus_rank0": len(local_cpus) if local_cpus else host_cores(),
                     "matches_device_decode": bool(e2e_ok)},
             "roofline": {"bound": "hbm", "kernel": f"fused decoder unit, class '{dom_name}'",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -245,14 +245,12 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
     constexpr int kChunksPerStep = kStagedElems / 4;
     const float dt = step_dt(a.steps);
     const bool in_prefix = active && (i % a.row) < a.prefix;
-    float x = active ? a.state[i] : 0.f;
-    const float nz = in_prefix ? a.noise[i] : 0.f;
-    const float cx = in_prefix ? a.ctx[i] : 0.f;
+    float x = 0.f, nz = 0.f, cx = 0.f;
     bool failed = false;
     for (int64_t k0 = 0; k0 < a.count; k0 += kStagedSteps) {
         const int cnt = static_cast<int>(a.count - k0 < kStagedSteps ? a.count - k0 : kStagedSteps);
-        __syncthreads();  // the previous round has been consumed
-        if (tid < kStagedElems) vfirst[tid] = INT_MAX;
+        if (k0 > 0) __syncthreads();  // the previous round has been consumed
+        // the copies go out first: nothing else stands between the launch and the DRAM requests
         {
             const int per_array = cnt * kChunksPerStep;
             const int total = a.cfg ? 2 * per_array : per_array;
@@ -265,6 +263,14 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
                     const float *src = (second ? a.c : a.u) + (k0 + st) * n + i0 + ch * 4;
                     cp_async16((second ? sc : su) + st * kStagedElems + ch * 4, src);
                 }
+            }
+        }
+        if (tid < kStagedElems) vfirst[tid] = INT_MAX;
+        if (k0 == 0 && active) {
+            x = a.state[i];
+            if (in_prefix) {
+                nz = a.noise[i];
+                cx = a.ctx[i];
             }
         }
         cp_async_wait_all();

@@ -41,6 +41,7 @@ class HostGather:
         self.rank = rank
         self.name = f"levo_b200_{tag}"
         self._pinned = False
+        self._pinned_base = 0
         self.shm = None
         self.path = None
         # POSIX shared memory when /dev/shm has room, else a file mapping in the temp dir.
@@ -75,21 +76,36 @@ class HostGather:
     def view(self, start: int, stop: int) -> np.ndarray:
         return self.array[start:stop]
 
-    def pin(self) -> bool:
-        """Page-locks the mapping for CUDA DMA; returns False when registration is refused."""
+    def pin(self, start: int = 0, stop: Optional[int] = None) -> bool:
+        """Page-locks the pages of windows [start, stop) (default: all) for CUDA DMA; returns False
+        when registration is refused.  This rank writes those pages first, so that under the kernel's
+        first-touch policy they are allocated on the memory node of the CPUs this rank runs on (see
+        bind_to_gpu_local_cpus) rather than all on the node of whichever rank touched them first:
+        with one GPU per rank, every GPU then copies its audio into memory local to it."""
         import torch
 
         if self._pinned:
             return True
-        rc = torch.cuda.cudart().cudaHostRegister(self.array.ctypes.data, self.nbytes, 0)
+        stop = self.shape[0] if stop is None else stop
+        if stop <= start:
+            return True
+        per_window = self.nbytes // self.shape[0]
+        page = os.sysconf("SC_PAGE_SIZE")
+        base = self.array.ctypes.data
+        lo = (base + start * per_window) // page * page
+        hi = -(-(base + stop * per_window) // page) * page
+        lo, hi = max(lo, base // page * page), min(hi, -(-(base + self.nbytes) // page) * page)
+        self.array[start:stop] = 0.0  # first touch by this rank
+        rc = torch.cuda.cudart().cudaHostRegister(lo, hi - lo, 0)
         self._pinned = int(rc) == 0
+        self._pinned_base = lo
         return self._pinned
 
     def close(self, barrier: Optional[Callable[[], None]] = None) -> None:
         if self._pinned:
             import torch
 
-            torch.cuda.cudart().cudaHostUnregister(self.array.ctypes.data)
+            torch.cuda.cudart().cudaHostUnregister(self._pinned_base)
             self._pinned = False
         self.array = None
         if barrier is not None:
@@ -122,6 +138,32 @@ def _free_bytes(path: str) -> int:
         return st.f_bavail * st.f_frsize
     except OSError:
         return 0
+
+
+def bind_to_gpu_local_cpus(device: int) -> Optional[list[int]]:
+    """Restricts this process to the CPUs NVML reports as local to GPU `device` (its NUMA node), so
+    its pinned host buffers are allocated next to that GPU's PCIe root.  Returns the CPUs, or None
+    when NVML is unavailable or reports no affinity (the process is left as it was).  Only this
+    process's CPU affinity changes; nothing of the GPU."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(device)
+            n_words = (os.cpu_count() + 63) // 64
+            mask = pynvml.nvmlDeviceGetCpuAffinity(handle, n_words)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:  # noqa: BLE001 - NVML missing or refusing: keep the current affinity
+        return None
+    cpus = [w * 64 + b for w, word in enumerate(mask) for b in range(64) if (int(word) >> b) & 1]
+    allowed = os.sched_getaffinity(0)
+    cpus = [c for c in cpus if c in allowed]
+    if not cpus:
+        return None
+    os.sched_setaffinity(0, cpus)
+    return cpus
 
 
 def run_tag() -> str:

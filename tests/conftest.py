@@ -88,7 +88,7 @@ def _log_error(record: dict) -> None:
             f.write(json.dumps(record) + "\n")
 
 
-def assert_close(got, want, tol: float, what: str = "", rel_tol="tol") -> None:
+def assert_close(got, want, tol: float, what: str = "", rel_tol="tol", terms=None) -> None:
     """Two bars on the finite elements:
       scaled   max |d| / max(|ref|, 1) <= tol;
       relative max |d| / |ref| <= rel_tol (default: tol; None skips it) on the elements with
@@ -97,8 +97,11 @@ def assert_close(got, want, tol: float, what: str = "", rel_tol="tol") -> None:
     leaves out values that are small only through cancellation (SnakeBeta's x + sin^2(ax)/b, a
     residual add, a LayerNorm beta): there a few-ulp difference in a term of size ~1, which any two
     F32 implementations of the reference's arithmetic have, reads as a large relative error of a
-    result near zero.  The relative error at the fixed floor |ref| >= 1e-3 is computed too and, with
-    LEVO_ERR_LOG set, every check appends both figures to that JSON-lines file."""
+    result near zero.  `terms` (same shape, optional): the magnitude of the terms the output sums
+    (e.g. |x| + |sin^2(ax)/b| for SnakeBeta); the relative error is then taken against
+    max(|ref|, terms) on every element, the relative error of the computation itself.  The relative
+    error at the fixed floor |ref| >= 1e-3 is computed too and, with LEVO_ERR_LOG set, every check
+    appends both figures to that JSON-lines file."""
     got = np.asarray(got)
     want = np.asarray(want)
     assert got.shape == want.shape, f"{what}: shape {got.shape} != {want.shape}"
@@ -108,7 +111,12 @@ def assert_close(got, want, tol: float, what: str = "", rel_tol="tol") -> None:
     err = scaled_error(g, w)
     rms = float(np.sqrt(np.mean(np.square(w, dtype=np.float64)))) if w.size else 0.0
     floor = REL_FLOOR_RMS * rms
-    rel = relative_error(g, w, floor)
+    if terms is not None:
+        scale = np.maximum(np.abs(w.astype(np.float64)), np.asarray(terms, dtype=np.float64)[m])
+        floor = 0.0
+        rel = float(np.max(np.abs(g.astype(np.float64) - w) / np.maximum(scale, 1e-30))) if w.size else 0.0
+    else:
+        rel = relative_error(g, w, floor)
     rel_fixed = relative_error(g, w, REL_FLOOR_FIXED)
     if rel_tol == "tol":
         rel_tol = tol

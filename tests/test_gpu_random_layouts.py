@@ -56,7 +56,12 @@ def test_fused_unit_random_layouts(ops, orc, dev, seed):
     ops.fused_unit_t(tu, g(b), tr, g(al), g(bl), x_out, y_out, tanh=tanh)
     xw, yw = orc.fused_unit(u, b, r, al, bl, tanh=tanh)
     what = f"c={c} t={t} mode={mode} offs={offs} res={has_res} bias={has_bias} snake={snake} tanh={tanh}"
-    assert_close(y_out.cpu().numpy(), yw, TOL, what)
+    # The output sums x = r + (u + b) and the snake term, then tanh (slope <= 1): relative error
+    # against the size of those terms (log-parameters ~ N(0, 0.3) make the snake term up to ~2.5x
+    # larger than a result that cancels towards zero).
+    pre = orc.fused_unit(u, b, r, al, bl, tanh=False)[1]
+    terms = np.abs(xw) + np.abs(pre - xw)
+    assert_close(y_out.cpu().numpy(), yw, TOL, what, terms=terms)
     if write_x:
         assert np.array_equal(x_out.cpu().numpy(), xw), what
 

@@ -89,3 +89,35 @@ def test_two_rank_gather(fail_rank, force_file):
         assert complete and good
     else:
         assert not complete  # rank 0 learns of the failure on the host, no partial result is accepted
+
+
+def test_bind_to_gpu_local_cpus_with_a_fake_nvml(pkg, monkeypatch):
+    """The rank is restricted to the CPUs NVML lists for its GPU (intersected with those it may use);
+    without NVML the affinity is left alone."""
+    import os
+    import sys
+    import types
+
+    sh = pkg.sharding
+    allowed = sorted(os.sched_getaffinity(0))
+    want = allowed[: max(1, len(allowed) // 2)]
+    mask = [0] * ((os.cpu_count() + 63) // 64)
+    for c in want:
+        mask[c // 64] |= 1 << (c % 64)
+    calls = {}
+    fake = types.SimpleNamespace(
+        nvmlInit=lambda: None, nvmlShutdown=lambda: None,
+        nvmlDeviceGetHandleByIndex=lambda i: calls.setdefault("device", i),
+        nvmlDeviceGetCpuAffinity=lambda h, n: mask[:n])
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    set_to = {}
+    monkeypatch.setattr(os, "sched_setaffinity", lambda pid, cpus: set_to.setdefault("cpus", list(cpus)))
+    assert sh.bind_to_gpu_local_cpus(3) == want
+    assert calls["device"] == 3 and set_to["cpus"] == want
+
+    def broken():
+        raise RuntimeError("NVML Shared Library Not Found")
+
+    monkeypatch.setitem(sys.modules, "pynvml", types.SimpleNamespace(nvmlInit=broken))
+    set_to.clear()
+    assert sh.bind_to_gpu_local_cpus(0) is None and not set_to
