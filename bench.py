@@ -69,6 +69,8 @@ def parse():
     p.add_argument("--no-tanh", action="store_true")
     p.add_argument("--only-kernels", action="store_true",
                    help="run only the configs 0-2 kernel suite (small; used for ncu captures)")
+    p.add_argument("--kernels", default="snakebeta,norms,weightnorm,euler",
+                   help="comma-separated subset of the kernel suite: snakebeta, norms, weightnorm, euler")
     return p.parse_args()
 
 
@@ -332,7 +334,7 @@ def input_sets(set_bytes: int) -> int:
     return max(3, -(-int(2.5 * L2_BYTES) // max(set_bytes, 1)))
 
 
-def kernel_suite(ops, dev, peak, steps, warmup):
+def kernel_suite(ops, dev, peak, steps, warmup, which=("snakebeta", "norms", "weightnorm", "euler")):
     """Configs 0-2 kernels.  `ms` is the per-launch time of KERNEL_LAUNCHES back-to-back launches,
     rotating over input sets larger than L2 in total, captured once into a CUDA graph and replayed
     between one pair of CUDA events (median of `steps` replays): device time, without the host
@@ -391,52 +393,59 @@ def kernel_suite(ops, dev, peak, steps, warmup):
                      "input_sets": len(fns), "bytes_touched_per_set": set_bytes,
                      "launches_per_timing": KERNEL_LAUNCHES, "ms_single_launch": timeit_single(fns[0]), **kw}
 
+    # Inputs are drawn in one fixed order whatever the subset, so every kernel sees the same data.
     # config 0: SnakeBeta F32 [128, 483840]
-    x = torch.from_numpy(rng.standard_normal((128, 483840), dtype=np.float32)).to(dev)
+    x = rng.standard_normal((128, 483840), dtype=np.float32)
     a = torch.from_numpy((0.1 * rng.standard_normal(128)).astype(np.float32)).to(dev)
     b = torch.from_numpy((0.1 * rng.standard_normal(128)).astype(np.float32)).to(dev)
-    set_bytes = 8 * x.numel()
-    sets = [(x if i == 0 else x.clone(), torch.empty_like(x)) for i in range(input_sets(set_bytes))]
-    entry_("snakebeta_f32[128,483840]", [lambda s=s: ops.snakebeta_t(s[0], a, b, out=s[1]) for s in sets],
-           8 * x.numel(), set_bytes)
-    del x, sets
+    if "snakebeta" in which:
+        x = torch.from_numpy(x).to(dev)
+        set_bytes = 8 * x.numel()
+        sets = [(x if i == 0 else x.clone(), torch.empty_like(x)) for i in range(input_sets(set_bytes))]
+        entry_("snakebeta_f32[128,483840]", [lambda s=s: ops.snakebeta_t(s[0], a, b, out=s[1]) for s in sets],
+               8 * x.numel(), set_bytes)
+        del sets
+    del x
     # config 1: add + RMSNorm / LayerNorm F16 [4096, 1536]; weight norm F32 [1024, 7168]
     xh = torch.from_numpy(rng.standard_normal((4096, 1536)).astype(np.float16)).to(dev)
     rh = torch.from_numpy(rng.standard_normal((4096, 1536)).astype(np.float16)).to(dev)
     g = torch.from_numpy((1 + 0.02 * rng.standard_normal(1536)).astype(np.float32)).to(dev)
     be = torch.from_numpy((0.02 * rng.standard_normal(1536)).astype(np.float32)).to(dev)
-    set_bytes = 8 * xh.numel()
-    sets = [(xh.clone(), rh.clone(), torch.empty_like(xh), torch.empty_like(xh))
-            for _ in range(input_sets(set_bytes))]
-    entry_("add_rmsnorm_f16[4096,1536]",
-           [lambda s=s: ops.add_rmsnorm_t(s[0], s[1], g, 1e-6, h_out=s[2], y_out=s[3]) for s in sets],
-           8 * xh.numel(), set_bytes)
-    entry_("add_layernorm_f16[4096,1536]",
-           [lambda s=s: ops.add_layernorm_t(s[0], s[1], g, be, 1e-5, h_out=s[2], y_out=s[3]) for s in sets],
-           8 * xh.numel(), set_bytes)
-    del sets
+    if "norms" in which:
+        set_bytes = 8 * xh.numel()
+        sets = [(xh.clone(), rh.clone(), torch.empty_like(xh), torch.empty_like(xh))
+                for _ in range(input_sets(set_bytes))]
+        entry_("add_rmsnorm_f16[4096,1536]",
+               [lambda s=s: ops.add_rmsnorm_t(s[0], s[1], g, 1e-6, h_out=s[2], y_out=s[3]) for s in sets],
+               8 * xh.numel(), set_bytes)
+        entry_("add_layernorm_f16[4096,1536]",
+               [lambda s=s: ops.add_layernorm_t(s[0], s[1], g, be, 1e-5, h_out=s[2], y_out=s[3]) for s in sets],
+               8 * xh.numel(), set_bytes)
+        del sets
     v = torch.from_numpy((0.02 * rng.standard_normal((1024, 7168))).astype(np.float32)).to(dev)
     gg = torch.from_numpy(rng.uniform(0.5, 1.5, 1024).astype(np.float32)).to(dev)
-    set_bytes = 8 * v.numel()
-    sets = [(v.clone(), torch.empty_like(v)) for _ in range(input_sets(set_bytes))]
-    entry_("weightnorm_f32[1024,7168]", [lambda s=s: ops.weightnorm_t(s[0], gg, w=s[1]) for s in sets],
-           8 * v.numel(), set_bytes)
-    del sets
+    if "weightnorm" in which:
+        set_bytes = 8 * v.numel()
+        sets = [(v.clone(), torch.empty_like(v)) for _ in range(input_sets(set_bytes))]
+        entry_("weightnorm_f32[1024,7168]", [lambda s=s: ops.weightnorm_t(s[0], gg, w=s[1]) for s in sets],
+               8 * v.numel(), set_bytes)
+        del sets
     # config 2: 50-step CFG + Euler on [2, 64, 252]
     n, S = 2 * 64 * 252, 50
     st0 = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).to(dev)
     vu = torch.from_numpy(rng.standard_normal((S, n)).astype(np.float32)).to(dev)
     vc = torch.from_numpy(rng.standard_normal((S, n)).astype(np.float32)).to(dev)
-    set_bytes = 4 * n * (2 * S + 2)
-    sets = [(st0.clone(), vu.clone(), vc.clone()) for _ in range(input_sets(set_bytes))]
-    entry_("cfg_euler_f32[2,64,252]x50",
-           [lambda s=s: ops.cfg_euler_multi_t(s[0], None, None, s[1], s[2], batch=2, prefix=0, first_step=0,
-                                              count=S, steps=S, guidance=1.5) for s in sets],
-           4 * n * (2 * S + 2), set_bytes, note="latency-bound: 13 MB")
-    del sets
+    if "euler" in which:
+        set_bytes = 4 * n * (2 * S + 2)
+        sets = [(st0.clone(), vu.clone(), vc.clone()) for _ in range(input_sets(set_bytes))]
+        entry_("cfg_euler_f32[2,64,252]x50",
+               [lambda s=s: ops.cfg_euler_multi_t(s[0], None, None, s[1], s[2], batch=2, prefix=0, first_step=0,
+                                                  count=S, steps=S, guidance=1.5) for s in sets],
+               4 * n * (2 * S + 2), set_bytes, note="latency-bound: 13 MB")
+        del sets
     # What a plain device copy of the same byte count reaches at these sizes (torch, not ours), timed
     # the same way: the achievable ceiling for ~50 MB kernels, where ramp-up and drain are a large share.
-    for mb in (50, 496):
+    for mb in (50, 496) if len(which) == 4 else (50,):
         src = torch.empty(mb * 1024 * 1024 // 8, dtype=torch.float32, device=dev)
         set_bytes = 2 * src.numel() * 4
         sets = [(src.clone(), torch.empty_like(src)) for _ in range(input_sets(set_bytes))]
@@ -450,7 +459,8 @@ def kernel_suite(ops, dev, peak, steps, warmup):
     copy_gbs = out["torch_copy_50MB_reference"]["GB/s"]
     for name in ("add_rmsnorm_f16[4096,1536]", "add_layernorm_f16[4096,1536]", "weightnorm_f32[1024,7168]",
                  "cfg_euler_f32[2,64,252]x50"):
-        out[name]["of_50MB_copy"] = out[name]["GB/s"] / copy_gbs
+        if name in out:
+            out[name]["of_50MB_copy"] = out[name]["GB/s"] / copy_gbs
     return out
 
 
@@ -615,7 +625,11 @@ def only_kernels(args):
     torch.cuda.set_device(dev)
     ops = entry.load_package().ops
     peak, _ = measured_peak()
-    emit({"kernels": kernel_suite(ops, dev, peak, steps=args.steps, warmup=args.warmup)})
+    which = tuple(k.strip() for k in args.kernels.split(",") if k.strip())
+    unknown = set(which) - {"snakebeta", "norms", "weightnorm", "euler"}
+    if unknown:
+        raise SystemExit(f"--kernels: unknown {sorted(unknown)}")
+    emit({"kernels": kernel_suite(ops, dev, peak, steps=args.steps, warmup=args.warmup, which=which)})
     return 0
 
 

@@ -537,6 +537,19 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
     return LEVO_OPS_OK;
 }
 
+// True when no value of p[0..n) is an infinity or a NaN: a branch-free OR over
+// the exponent fields, which the compiler vectorises (a window's latent is
+// 192 KB at 750 frames).
+bool finite_values(const float *p, int64_t n) {
+    uint32_t bad = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        uint32_t bits;
+        std::memcpy(&bits, p + i, sizeof(bits));
+        bad |= static_cast<uint32_t>((bits & 0x7f800000u) == 0x7f800000u);
+    }
+    return bad == 0;
+}
+
 int check_decode_args(levo_vae_chain *c, int64_t frames, uint32_t flags, const char *what) {
     if (c == nullptr) return set_error(LEVO_OPS_EINVAL, std::string(what) + ": chain is null");
     if (frames <= 0 || frames > c->max_frames)
@@ -757,6 +770,10 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
     const int64_t audio_elems = static_cast<int64_t>(t.audio_channels) * frames * total_upsampling(t);
     bool pending[2] = {false, false};
     cudaError_t err = cudaSuccess;
+    auto non_finite = [](int64_t window) {
+        return set_error(LEVO_OPS_ENONFINITE, "levo_vae_chain_decode_windows: latent payload contains a non-finite "
+                                              "value (window " + std::to_string(window) + ")");
+    };
     // Every exit waits for both streams: no copy of this call may still be
     // writing into audio_host once the call has returned.
     auto drained = [&](int rc) {
@@ -768,13 +785,13 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
         if (cancel != nullptr && cancel(cancel_user) != 0)
             return drained(set_error(LEVO_OPS_ECANCELLED,
                                      "levo_vae_chain_decode_windows: cancelled before window " + std::to_string(w)));
-        // vae_decoder::decode rejects non-finite latents before any work (src/levo-vae.cpp:189-191)
+        // vae_decoder::decode rejects non-finite latents (src/levo-vae.cpp:189-191).  The check runs on
+        // the host while the GPU already decodes the window, and before the window's audio copy is
+        // enqueued, so a rejected window still writes nothing to audio_host; with stage capture it
+        // runs first, as nothing may reach the capture buffers either.
         const float *lat_w = latents_host + w * lat_elems;
-        for (int64_t i = 0; i < lat_elems; ++i) {
-            if (!std::isfinite(lat_w[i]))
-                return drained(set_error(LEVO_OPS_ENONFINITE, "levo_vae_chain_decode_windows: latent payload contains "
-                                                              "a non-finite value (window " + std::to_string(w) + ")"));
-        }
+        const bool check_first = chain->n_capture > 0;
+        if (check_first && !finite_values(lat_w, lat_elems)) return drained(non_finite(w));
         const int slot = static_cast<int>(w & 1);
         // The slot's previous audio must have left the device before reuse.
         if (pending[slot]) err = cudaStreamWaitEvent(s, chain->copied[slot], 0);
@@ -784,6 +801,7 @@ LEVO_OPS_API int levo_vae_chain_decode_windows(levo_vae_chain *chain, const floa
         if (err != cudaSuccess) return drained(cuda_fail(err, "levo_vae_chain_decode_windows: latent upload"));
         rc = decode_one(chain, chain->lat[slot], frames, chain->audio[slot], flags, s);
         if (rc != LEVO_OPS_OK) return drained(rc);
+        if (!check_first && !finite_values(lat_w, lat_elems)) return drained(non_finite(w));
         err = cudaEventRecord(chain->computed[slot], s);
         if (err == cudaSuccess) err = cudaStreamWaitEvent(chain->copy_stream, chain->computed[slot], 0);
         if (err == cudaSuccess)
