@@ -250,18 +250,19 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
     for (int64_t k0 = 0; k0 < a.count; k0 += kStagedSteps) {
         const int cnt = static_cast<int>(a.count - k0 < kStagedSteps ? a.count - k0 : kStagedSteps);
         if (k0 > 0) __syncthreads();  // the previous round has been consumed
-        // the copies go out first: nothing else stands between the launch and the DRAM requests
+        // the copies go out first: nothing else stands between the launch and the DRAM requests.
+        // Thread t copies chunk t % 16 of step rows t / 16, + 16, ... of both arrays (no division
+        // inside the loop).
         {
-            const int per_array = cnt * kChunksPerStep;
-            const int total = a.cfg ? 2 * per_array : per_array;
-            for (int idx = tid; idx < total; idx += kStagedThreads) {
-                const bool second = idx >= per_array;
-                const int rem = second ? idx - per_array : idx;
-                const int st = rem / kChunksPerStep;
-                const int ch = rem % kChunksPerStep;
-                if (ch < chunks_valid) {
-                    const float *src = (second ? a.c : a.u) + (k0 + st) * n + i0 + ch * 4;
-                    cp_async16((second ? sc : su) + st * kStagedElems + ch * 4, src);
+            constexpr int kRowsPerPass = kStagedThreads / kChunksPerStep;
+            const int ch = tid % kChunksPerStep;
+            if (ch < chunks_valid) {
+                const int64_t col = i0 + ch * 4;
+                const float *bu = a.u + k0 * n + col;
+                const float *bc = a.cfg ? a.c + k0 * n + col : nullptr;
+                for (int st = tid / kChunksPerStep; st < cnt; st += kRowsPerPass) {
+                    cp_async16(su + st * kStagedElems + ch * 4, bu + st * n);
+                    if (a.cfg) cp_async16(sc + st * kStagedElems + ch * 4, bc + st * n);
                 }
             }
         }
