@@ -326,6 +326,45 @@ struct Chunk<__half> {
     __device__ static float first(const uint4 &c) {
         return __half2float(__ushort_as_half(static_cast<unsigned short>(c.x & 0xffffu)));
     }
+    // sm_100 mixed-precision forms: the F16 halves of a word enter the F32 arithmetic directly
+    // (the product of two F16 values is exact in F32, so fma.f32.f16 rounds once, like an F32 FMA
+    // of the converted values; add.f32.f16 likewise equals the F32 add of the converted value).
+    __device__ static void halves(uint32_t w, unsigned short &lo, unsigned short &hi) {
+        asm("mov.b32 {%0, %1}, %2;" : "=h"(lo), "=h"(hi) : "r"(w));
+    }
+    __device__ static float sq_add(unsigned short h, float c) {
+        float d;
+        asm("fma.rn.f32.f16 %0, %1, %1, %2;" : "=f"(d) : "h"(h), "f"(c));
+        return d;
+    }
+    __device__ static float add_f32(unsigned short h, float c) {
+        float d;
+        asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(h), "f"(c));
+        return d;
+    }
+    // sum of squares of the chunk, even and odd columns in two accumulators (as a paired FFMA2)
+    __device__ static float sq_sum(const uint4 &c) {
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        float ax = 0.f, ay = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            unsigned short lo, hi;
+            halves(w[i], lo, hi);
+            ax = sq_add(lo, ax);
+            ay = sq_add(hi, ay);
+        }
+        return ax + ay;
+    }
+    // (h - k) for the chunk's values, in column pairs
+    __device__ static void minus(const uint4 &c, float k, float2 *d) {
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            unsigned short lo, hi;
+            halves(w[i], lo, hi);
+            d[i] = make_float2(add_f32(lo, -k), add_f32(hi, -k));
+        }
+    }
     // x + r rounded to F16 in one HADD2 per pair.  The F32 sum of two F16
     // values rounded to F16 is the same number: F32 carries 24 >= 2*11 + 1
     // significand bits, so the double rounding is innocuous (S. A. Figueroa,
@@ -346,6 +385,17 @@ template <>
 struct Chunk<float> {
     static constexpr int kN = 4;
     __device__ static float first(const uint4 &c) { return __uint_as_float(c.x); }
+    __device__ static float sq_sum(const uint4 &c) {
+        const float2 v0 = make_float2(__uint_as_float(c.x), __uint_as_float(c.y));
+        const float2 v1 = make_float2(__uint_as_float(c.z), __uint_as_float(c.w));
+        float2 acc = __ffma2_rn(v0, v0, make_float2(0.f, 0.f));
+        acc = __ffma2_rn(v1, v1, acc);
+        return acc.x + acc.y;
+    }
+    __device__ static void minus(const uint4 &c, float k, float2 *d) {
+        d[0] = __fadd2_rn(make_float2(__uint_as_float(c.x), __uint_as_float(c.y)), pair(-k));
+        d[1] = __fadd2_rn(make_float2(__uint_as_float(c.z), __uint_as_float(c.w)), pair(-k));
+    }
     __device__ static void unpack(const uint4 &c, float *v) {
         v[0] = __uint_as_float(c.x);
         v[1] = __uint_as_float(c.y);
@@ -539,16 +589,17 @@ __device__ __forceinline__ uint4 norm_chunk_out(uint4 hc, const float4 *gs, cons
                                                 float scale) {
     constexpr int N = Chunk<T>::kN;
     float h[N];
-    Chunk<T>::unpack(hc, h);
+    float2 dm[N / 2];
+    if (LAYER) {
+        Chunk<T>::minus(hc, mean, dm);  // h - mean, the reference's first rounded step
+    } else {
+        Chunk<T>::unpack(hc, h);
+    }
 #pragma unroll
     for (int q = 0; q < N / 4; ++q) {
         const float4 g = gs[i * (N / 4) + q];
-        float2 v0 = make_float2(h[4 * q], h[4 * q + 1]);
-        float2 v1 = make_float2(h[4 * q + 2], h[4 * q + 3]);
-        if (LAYER) {
-            v0 = __fadd2_rn(v0, pair(-mean));
-            v1 = __fadd2_rn(v1, pair(-mean));
-        }
+        float2 v0 = LAYER ? dm[2 * q] : make_float2(h[4 * q], h[4 * q + 1]);
+        float2 v1 = LAYER ? dm[2 * q + 1] : make_float2(h[4 * q + 2], h[4 * q + 3]);
         v0 = __fmul2_rn(v0, pair(scale));
         v1 = __fmul2_rn(v1, pair(scale));
         if (BOUND) {
@@ -568,21 +619,6 @@ __device__ __forceinline__ uint4 norm_chunk_out(uint4 hc, const float4 *gs, cons
         h[4 * q + 3] = v1.y;
     }
     return Chunk<T>::pack(h);
-}
-
-// Paired partial sum of one chunk (sum of values for LayerNorm, of squares for RMSNorm).
-template <typename T, bool LAYER>
-__device__ __forceinline__ float chunk_sum(uint4 hc) {
-    constexpr int N = Chunk<T>::kN;
-    float h[N];
-    Chunk<T>::unpack(hc, h);
-    float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int j = 0; j < N; j += 2) {
-        const float2 v = make_float2(h[j], h[j + 1]);
-        acc = LAYER ? __fadd2_rn(acc, v) : __ffma2_rn(v, v, acc);
-    }
-    return acc.x + acc.y;
 }
 
 template <typename T, bool LAYER, bool BOUND, int CPL>
@@ -670,13 +706,12 @@ __global__ void __launch_bounds__(kRegsWarps * 32, 4) add_norm_regs_kernel(const
 #pragma unroll
             for (int k = 0; k < CPL; ++k) {
                 if (k < mine) {
-                    float h[N];
-                    Chunk<T>::unpack(hreg[k], h);
+                    float2 d[N / 2];
+                    Chunk<T>::minus(hreg[k], K, d);
 #pragma unroll
-                    for (int j = 0; j < N; j += 2) {
-                        const float2 d = __fadd2_rn(make_float2(h[j], h[j + 1]), pair(-K));
-                        s1 = __fadd2_rn(s1, d);
-                        s2 = __ffma2_rn(d, d, s2);
+                    for (int j = 0; j < N / 2; ++j) {
+                        s1 = __fadd2_rn(s1, d[j]);
+                        s2 = __ffma2_rn(d[j], d[j], s2);
                     }
                 }
             }
@@ -693,7 +728,7 @@ __global__ void __launch_bounds__(kRegsWarps * 32, 4) add_norm_regs_kernel(const
         } else {
 #pragma unroll
             for (int k = 0; k < CPL; ++k)
-                if (k < mine) sum += chunk_sum<T, LAYER>(hreg[k]);
+                if (k < mine) sum += Chunk<T>::sq_sum(hreg[k]);
             sum = warp_sum(sum);
             scale = 1.0f / sqrtf(sum * inv_dim + a.eps);
         }
