@@ -3,7 +3,8 @@
 // One CTA per row, one HBM read of v and one write of w (8 B per element):
 //  * rows up to kMaxStagedCols values are copied into shared memory with
 //    cp.async (a 1024 x 7168 weight: 28 KB per CTA, 7 CTAs per SM, the whole
-//    tensor in flight in one wave), reduced from there and scaled out;
+//    tensor in flight in one wave), reduced from there and scaled out, in
+//    passes unrolled over a compile-time chunk count per thread;
 //  * longer rows up to 16384 values stay in registers, longer still are
 //    streamed twice (the second read mostly hits L2).  The arithmetic follows the reference's numpy
 // expression (convert/convert_vae.py:196-199): norm = sqrt(sum(v*v)) in F32,
@@ -97,36 +98,97 @@ __global__ void __launch_bounds__(256) weightnorm_vec_kernel(const WnArgs a) {
 }
 
 constexpr int64_t kMaxStagedCols = 12032;  // <= 48 KB of shared memory per CTA with red[]
+constexpr int kStagedThreads = 128;
+constexpr int kStagedMaxCpt = (kMaxStagedCols / 4 + kStagedThreads - 1) / kStagedThreads;  // 24
 
-__global__ void __launch_bounds__(128) weightnorm_staged_kernel(const WnArgs a) {
+constexpr int kStagedRowsPerCta = 2;  // rows per CTA a launch aims for (the next row's copy overlaps)
+
+// CPT: 16-byte chunks per thread (compile time).  The row is copied into shared
+// memory with cp.async, then read into registers in one unrolled burst; as
+// soon as every thread holds its chunks the buffer takes the CTA's next row's
+// copies, which overlap this row's reduction and output.  The grid aims at
+// about kStagedRowsPerCta rows per CTA in whole CTAs per SM.
+template <int CPT>
+__global__ void __launch_bounds__(kStagedThreads, 4) weightnorm_staged_kernel(const WnArgs a) {
     extern __shared__ float4 row_buf[];
     __shared__ float red[32];
-    const int64_t nchunk = a.cols / 4;
-    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int nchunk = static_cast<int>(a.cols / 4);
+    const int t = threadIdx.x;
+    auto issue = [&](int64_t row) {
         const float4 *vr = reinterpret_cast<const float4 *>(a.v + row * a.cols);
-        float4 *wr = reinterpret_cast<float4 *>(a.w + row * a.cols);
-        __syncthreads();  // row_buf is reused across rows
-        for (int64_t i = threadIdx.x; i < nchunk; i += blockDim.x) cp_async16(row_buf + i, vr + i);
-        cp_async_wait_all();
-        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+            const int i = t + kStagedThreads * k;
+            if (i < nchunk) cp_async16(row_buf + i, vr + i);
+        }
+    };
+    int64_t row = blockIdx.x;
+    if (row < a.rows) issue(row);
+    cp_async_commit();
+    for (; row < a.rows; row += gridDim.x) {
+        cp_async_wait_group<0>();
+        __syncthreads();  // the row is in shared memory
+        float4 b[CPT];
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+            const int i = t + kStagedThreads * k;
+            if (i < nchunk) b[k] = row_buf[i];
+        }
+        __syncthreads();  // every thread holds its chunks: the buffer takes the next row
+        const int64_t next = row + gridDim.x;
+        if (next < a.rows) issue(next);
+        cp_async_commit();
         float s = 0.f;
-        for (int64_t i = threadIdx.x; i < nchunk; i += blockDim.x) {
-            const float4 b = row_buf[i];
-            s = fmaf(b.x, b.x, s);
-            s = fmaf(b.y, b.y, s);
-            s = fmaf(b.z, b.z, s);
-            s = fmaf(b.w, b.w, s);
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+            if (t + kStagedThreads * k < nchunk) {
+                s = fmaf(b[k].x, b[k].x, s);
+                s = fmaf(b[k].y, b[k].y, s);
+                s = fmaf(b[k].z, b[k].z, s);
+                s = fmaf(b[k].w, b[k].w, s);
+            }
         }
         const float scale = row_scale(a, row, block_sum(s, red));
-        for (int64_t i = threadIdx.x; i < nchunk; i += blockDim.x) {
-            float4 b = row_buf[i];
-            b.x = __fmul_rn(b.x, scale);
-            b.y = __fmul_rn(b.y, scale);
-            b.z = __fmul_rn(b.z, scale);
-            b.w = __fmul_rn(b.w, scale);
-            wr[i] = b;
+        float4 *wr = reinterpret_cast<float4 *>(a.w + row * a.cols);
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+            const int i = t + kStagedThreads * k;
+            if (i < nchunk)
+                wr[i] = make_float4(__fmul_rn(b[k].x, scale), __fmul_rn(b[k].y, scale), __fmul_rn(b[k].z, scale),
+                                    __fmul_rn(b[k].w, scale));
         }
     }
+    cp_async_wait_group<0>();  // nothing of this thread's is left in flight at exit
+}
+
+template <int CPT>
+void run_staged(const WnArgs &a, cudaStream_t stream) {
+    auto kernel = weightnorm_staged_kernel<CPT>;
+    const size_t smem = static_cast<size_t>(a.cols) * sizeof(float);
+    int resident = 0;
+    if (resident_ctas(reinterpret_cast<const void *>(kernel), kStagedThreads, smem, &resident) != cudaSuccess ||
+        resident <= 0) {
+        cudaGetLastError();
+        resident = 1;
+    }
+    const int64_t sms = sm_count();
+    int64_t per_sm = (a.rows + sms * kStagedRowsPerCta - 1) / (sms * kStagedRowsPerCta);
+    per_sm = std::min<int64_t>(std::max<int64_t>(per_sm, 1), resident);
+    const int64_t grid = std::min<int64_t>(a.rows, sms * per_sm);
+    kernel<<<static_cast<unsigned>(grid), kStagedThreads, smem, stream>>>(a);
+}
+
+// The smallest instantiated chunk count that covers the row (cpt <= kStagedMaxCpt).
+void launch_staged(const WnArgs &a, int cpt, cudaStream_t stream) {
+    if (cpt <= 1) return run_staged<1>(a, stream);
+    if (cpt <= 2) return run_staged<2>(a, stream);
+    if (cpt <= 4) return run_staged<4>(a, stream);
+    if (cpt <= 6) return run_staged<6>(a, stream);
+    if (cpt <= 8) return run_staged<8>(a, stream);
+    if (cpt <= 12) return run_staged<12>(a, stream);
+    if (cpt <= 14) return run_staged<14>(a, stream);
+    if (cpt <= 16) return run_staged<16>(a, stream);
+    return run_staged<kStagedMaxCpt>(a, stream);
 }
 
 // Any row length / alignment.
@@ -174,10 +236,8 @@ LEVO_OPS_API int levo_weightnorm_f32(const float *v, const float *g, float *w, f
         weightnorm_scalar_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(a);
         return check_launch("levo_weightnorm_f32");
     }
-    if (cols <= kMaxStagedCols && cols % 4 == 0 && aligned_to(v, 16) && aligned_to(w, 16)) {
-        const size_t smem = static_cast<size_t>(cols) * sizeof(float);
-        const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * 16);
-        weightnorm_staged_kernel<<<static_cast<unsigned>(grid), 128, smem, s>>>(a);
+    if (staged) {
+        launch_staged(a, static_cast<int>((cols / 4 + kStagedThreads - 1) / kStagedThreads), s);
         return check_launch("levo_weightnorm_f32");
     }
     const int64_t nvec = cols / 8;
