@@ -42,6 +42,16 @@ __device__ __forceinline__ void prefix_times(int64_t step, float dt, float sigma
     ns = __fsub_rn(1.0f, __fmul_rn(__fsub_rn(1.0f, sigma_min), t));
 }
 
+// Whether element i of a [batch][row] state lies in its row's in-context prefix.  No
+// division at all without a prefix, a 32-bit one when the indices fit (a 64-bit
+// remainder is a long instruction sequence).
+__device__ __forceinline__ bool in_context_prefix(int64_t i, int64_t row, int64_t prefix) {
+    if (prefix <= 0) return false;
+    if (i <= INT32_MAX && row <= INT32_MAX)
+        return static_cast<int64_t>(static_cast<uint32_t>(i) % static_cast<uint32_t>(row)) < prefix;
+    return (i % row) < prefix;
+}
+
 __device__ __forceinline__ void flag_status(int32_t *status, int bits) {
     if (status && bits) atomicOr(status, bits);
 }
@@ -164,7 +174,7 @@ __global__ void __launch_bounds__(kThreads) euler_multi_kernel(const MultiArgs a
     const float dt = step_dt(a.steps);
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const bool in_prefix = (i % a.row) < a.prefix;
+        const bool in_prefix = in_context_prefix(i, a.row, a.prefix);
         float x = a.state[i];
         const float nz = in_prefix ? a.noise[i] : 0.f;
         const float cx = in_prefix ? a.ctx[i] : 0.f;
@@ -213,15 +223,17 @@ __global__ void __launch_bounds__(kThreads) euler_multi_kernel(const MultiArgs a
 // with cp.async in one burst (all of config 2's 13 MB is in flight at once).
 // Then, per round:
 //   velocity phase: four threads per element (steps q, q + 4, ...) form the CFG
-//     combine, note the first non-finite velocity and replace u by dt * v in
-//     place (the reference rounds dt * v before adding it, so x + w is its
-//     x + dt * v bit for bit);
+//     combine and replace u by dt * v in place (the reference rounds dt * v
+//     before adding it, so x + w is its x + dt * v bit for bit);
 //   chain phase: one thread per element runs the dependent x = x + w (after
-//     the in-context interpolation for prefix elements) up to that step.
-// Outside the prefix a non-finite state stays non-finite (w is finite), so the
-// chain checks the state once at the end and replays the round with per-step
-// checks only when it failed; prefix elements, re-interpolated every step,
-// check every step.
+//     the in-context interpolation for prefix elements).
+// No step is checked on the way.  dt = 1 / steps lies in (0, 1], so w is
+// non-finite exactly when v is, and outside the prefix a state that turned
+// non-finite (through w or an overflow) stays so: the chain checks x once at
+// the end of the round and, only when it failed, replays the round from its
+// start with the reference's per-step checks, velocity first, to find the
+// step and the kind.  Prefix elements, re-interpolated every step, always
+// take the checked replay.
 constexpr int kStagedElems = 64;
 constexpr int kStagedLanes = 4;
 constexpr int kStagedThreads = kStagedElems * kStagedLanes;
@@ -229,7 +241,6 @@ constexpr int kStagedSteps = 64;
 
 __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(const MultiArgs a) {
     extern __shared__ float4 stage[];  // [2][kStagedSteps][kStagedElems] F32: u (then dt * v), c
-    __shared__ int vfirst[kStagedElems];
     float *su = reinterpret_cast<float *>(stage);
     float *sc = su + kStagedSteps * kStagedElems;
     const int64_t n = a.batch * a.row;
@@ -244,7 +255,7 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
     const int chunks_valid = valid / 4;
     constexpr int kChunksPerStep = kStagedElems / 4;
     const float dt = step_dt(a.steps);
-    const bool in_prefix = active && (i % a.row) < a.prefix;
+    const bool in_prefix = active && in_context_prefix(i, a.row, a.prefix);
     float x = 0.f, nz = 0.f, cx = 0.f;
     bool failed = false;
     for (int64_t k0 = 0; k0 < a.count; k0 += kStagedSteps) {
@@ -266,7 +277,6 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
                 }
             }
         }
-        if (tid < kStagedElems) vfirst[tid] = INT_MAX;
         if (k0 == 0 && active) {
             x = a.state[i];
             if (in_prefix) {
@@ -280,42 +290,45 @@ __global__ void __launch_bounds__(kStagedThreads) euler_multi_staged_kernel(cons
             for (int st = q; st < cnt; st += kStagedLanes) {
                 const float u = su[st * kStagedElems + e];
                 const float v = a.cfg ? cfg_mix(u, sc[st * kStagedElems + e], a.g) : u;
-                if (!isfinite(v)) atomicMin(&vfirst[e], st);
                 su[st * kStagedElems + e] = __fmul_rn(dt, v);
             }
         }
         __syncthreads();
         if (active && !failed) {
-            const int kv = vfirst[tid];
-            const int run = kv < cnt ? kv : cnt;
-            int fail_st = kv < cnt ? kv : -1;
-            int kind = 3;
             const float x0 = x;
             if (!in_prefix) {
 #pragma unroll 8
-                for (int st = 0; st < run; ++st) x = __fadd_rn(x, su[st * kStagedElems + tid]);
+                for (int st = 0; st < cnt; ++st) x = __fadd_rn(x, su[st * kStagedElems + tid]);
             }
+            // Rare path: the round replayed from x0 with the reference's per-step checks.  With
+            // 0 < dt <= 1, w = dt * v is non-finite exactly when v is, so a non-finite velocity
+            // leaves x non-finite too, and outside the prefix (no re-interpolation) a non-finite
+            // x stays so: one check after the plain chain finds every failing round.
             if (in_prefix || !isfinite(x)) {
                 x = x0;
-                for (int st = 0; st < run; ++st) {
-                    float xs = x;
-                    if (in_prefix) {
-                        float t, ns;
-                        prefix_times(a.first + k0 + st, dt, a.sigma_min, t, ns);
-                        xs = __fadd_rn(__fmul_rn(ns, nz), __fmul_rn(t, cx));
+                for (int st = 0; st < cnt; ++st) {
+                    const float w = su[st * kStagedElems + tid];
+                    int kind = 0;
+                    float nx = x;
+                    if (!isfinite(w)) {
+                        kind = LEVO_EULER_FAIL_VELOCITY;
+                    } else {
+                        float xs = x;
+                        if (in_prefix) {
+                            float t, ns;
+                            prefix_times(a.first + k0 + st, dt, a.sigma_min, t, ns);
+                            xs = __fadd_rn(__fmul_rn(ns, nz), __fmul_rn(t, cx));
+                        }
+                        nx = __fadd_rn(xs, w);
+                        if (!isfinite(nx)) kind = LEVO_EULER_FAIL_STATE;
                     }
-                    const float nx = __fadd_rn(xs, su[st * kStagedElems + tid]);
-                    if (!isfinite(nx)) {
-                        fail_st = st;
-                        kind = 2;
+                    if (kind != 0) {
+                        failed = true;
+                        record_failure(a.status, a.first + k0 + st, kind);
                         break;
                     }
                     x = nx;
                 }
-            }
-            if (fail_st >= 0) {
-                failed = true;
-                record_failure(a.status, a.first + k0 + fail_st, kind);
             }
         }
     }
