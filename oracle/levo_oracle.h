@@ -58,7 +58,15 @@ int oracle_vae_chain_stages_f32(const int32_t *topology, const float *params, co
 
 /* Residual add + RMSNorm / LayerNorm on F16 (IEEE half bits) or F32 rows.
  * RMSNorm: src/levo-lm.cpp:131-138, src/levo-kv.cpp:153-170.
- * LayerNorm: src/levo-flow-estimator.cpp:106-109.  r / h_out may be NULL. */
+ * LayerNorm: src/levo-flow-estimator.cpp:106-109.  r / h_out may be NULL.
+ * PARITY UNPINNED against the reference itself: its norms are the GGML nodes
+ * ggml_rms_norm / ggml_norm, and GGML (the reference's `ggml` submodule, whose
+ * commit this tree does not record) is absent.  The restatement follows GGML's
+ * published CPU algorithm (row statistics accumulated in double, the scale
+ * 1/sqrt(stat + eps) in F32, then separate gamma / beta nodes) and is checked
+ * against the float64 definitions and against the upstream modules the
+ * reference's parity policy gates its norms against (tests/golden/
+ * make_norm_golden.py: Transformers' Llama RMSNorm, torch's LayerNorm). */
 int oracle_add_rmsnorm_f16(const uint16_t *x, const uint16_t *r, const float *gamma,
                            uint16_t *h_out, uint16_t *y_out, int64_t rows, int64_t dim, float eps,
                            int f16_boundary, int threads);

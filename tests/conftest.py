@@ -126,3 +126,41 @@ def assert_close(got, want, tol: float, what: str = "", rel_tol="tol", terms=Non
     assert err <= tol, f"{what}: max scaled error {err:.3g} > {tol:g}"
     if rel_tol is not None:
         assert rel <= rel_tol, f"{what}: max relative error {rel:.3g} > {rel_tol:g} (|ref| >= {floor:.3g})"
+
+
+# --------------------------------------------------------------------------- upstream norm fixtures
+
+UPSTREAM_NORM_CASES = ("rms_f32", "rms_f16", "ln_f32", "ln_f16")
+
+
+def upstream_norm_case(name: str) -> dict:
+    """One case of tests/golden/norms_upstream.npz (tests/golden/make_norm_golden.py): inputs x, r,
+    weight w (and bias b for LayerNorm) in the activation dtype, the upstream module's output y,
+    and h = x + r rounded to the activation dtype."""
+    z = np.load(GOLDEN / "norms_upstream.npz")
+    case = {k[len(name) + 1:]: z[k] for k in z.files if k.startswith(name + "_")}
+    case["h"] = case["x"] + case["r"]
+    case["layer"] = name.startswith("ln")
+    case["half"] = case["x"].dtype == np.float16
+    return case
+
+
+def assert_upstream_gates(got, want, what: str) -> None:
+    """The reference's own parity gates against the upstream modules (docs/parity.md:16-18):
+    F32 atol = rtol = 1e-4; F16 cosine similarity >= 0.9999 and normalised RMSE <= 1e-2.  F16
+    results must also stay within one F16 ulp of the upstream value on every element (the two
+    differ only in the F32 rounding of the statistics before the final F16 rounding), the ulp taken
+    at max(|ref|, 0.05 RMS(ref)) like the relative bar of assert_close: a LayerNorm output that is
+    small only because + beta cancels the normalised term carries the error of that term."""
+    g = np.asarray(got).astype(np.float64)
+    w = np.asarray(want).astype(np.float64)
+    if np.asarray(want).dtype == np.float16:
+        cos = float(np.sum(g * w) / np.sqrt(np.sum(g * g) * np.sum(w * w)))
+        nrmse = float(np.sqrt(np.mean((g - w) ** 2)) / np.sqrt(np.mean(w * w)))
+        floor = REL_FLOOR_RMS * float(np.sqrt(np.mean(w * w)))
+        ulp = np.spacing(np.maximum(np.abs(np.asarray(want)), np.float16(floor))).astype(np.float64)
+        assert cos >= 0.9999, f"{what}: cosine {cos}"
+        assert nrmse <= 1e-2, f"{what}: normalised RMSE {nrmse}"
+        assert np.all(np.abs(g - w) <= ulp), f"{what}: {int(np.sum(np.abs(g - w) > ulp))} values beyond 1 F16 ulp"
+    else:
+        assert np.allclose(g, w, rtol=1e-4, atol=1e-4), f"{what}: beyond atol = rtol = 1e-4"

@@ -4,7 +4,10 @@ fold (a9) against the oracle, through the C ABI.
 Tolerances: F16-boundary norms 2e-3 scaled error (north_star), F32 norms and
 weight norm 1e-5.  h = x + r is rounded identically on both sides: bit-exact.
 RMSNorm / LayerNorm parity is unpinned against the reference itself (its tests
-only check shapes and finiteness); weight norm is pinned by the fixtures of
+only check shapes and finiteness; its norms are GGML nodes and GGML is absent):
+they are anchored on the upstream modules the reference's parity policy holds
+them to (Transformers' Llama RMSNorm, torch's LayerNorm; fixtures from
+tests/golden/make_norm_golden.py).  Weight norm is pinned by the fixtures of
 the reference converters."""
 from __future__ import annotations
 
@@ -12,7 +15,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, assert_close
+from conftest import GOLDEN, UPSTREAM_NORM_CASES, assert_close, assert_upstream_gates, upstream_norm_case
 
 pytestmark = pytest.mark.gpu
 
@@ -42,6 +45,25 @@ def test_add_norm_matches_oracle(ops, orc, dev, layer, dt, dim):
         hw, yw = orc.add_rmsnorm(x, r, g, eps)
     assert np.array_equal(h.cpu().numpy(), hw)
     assert_close(y.cpu().numpy().astype(np.float64), yw.astype(np.float64), 2e-3 if dt == np.float16 else 1e-5)
+
+
+@pytest.mark.parametrize("name", UPSTREAM_NORM_CASES)
+def test_add_norm_matches_upstream_modules(ops, dev, name):
+    """The CUDA norms against the upstream modules the reference's parity policy holds its norms to
+    (tests/golden/norms_upstream.npz): the reference's own gates and north_star's bars.  dim 1536
+    (F16 and F32) runs the register form, dim 2200 the staged form."""
+    c = upstream_norm_case(name)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    w = T(c["w"].astype(np.float32))
+    if c["layer"]:
+        h, y = ops.add_layernorm_t(T(c["x"]), T(c["r"]), w, T(c["b"].astype(np.float32)), 1e-5)
+    else:
+        h, y = ops.add_rmsnorm_t(T(c["x"]), T(c["r"]), w, 1e-5, f16_boundary=c["half"])
+    y = y.cpu().numpy()
+    assert np.array_equal(h.cpu().numpy(), c["h"])
+    assert_upstream_gates(y, c["y"], name)
+    if not c["half"]:
+        assert_close(y.astype(np.float64), c["y"].astype(np.float64), 1e-5, name)
 
 
 @pytest.mark.parametrize("layer", [False, True])

@@ -13,7 +13,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, assert_close
+from conftest import GOLDEN, UPSTREAM_NORM_CASES, assert_close, assert_upstream_gates, upstream_norm_case
 
 
 # --------------------------------------------------------------------------- SnakeBeta
@@ -92,7 +92,7 @@ def test_weightnorm_zero_norm_is_an_error(orc):
     assert not ok and norms[1] == 0
 
 
-# --------------------------------------------------------------------------- norms (unpinned)
+# --------------------------------------------------------------------------- norms (unpinned against the reference itself; anchored on the upstream modules below)
 
 @pytest.mark.parametrize("half", [False, True])
 def test_rmsnorm_matches_definition(orc, half):
@@ -121,6 +121,27 @@ def test_layernorm_matches_definition(orc, half):
     mu = hh.mean(axis=1, keepdims=True)
     want = (hh - mu) / np.sqrt(((hh - mu) ** 2).mean(axis=1, keepdims=True) + 1e-5) * g + b
     assert_close(y.astype(np.float64), want, 2e-3 if half else 1e-5)
+
+
+@pytest.mark.parametrize("name", UPSTREAM_NORM_CASES)
+def test_norms_match_upstream_modules(orc, name):
+    """The oracle against the upstream modules the reference's parity policy holds its norms to
+    (Transformers' Llama RMSNorm for the LM, torch's LayerNorm for the Flow estimator;
+    tests/golden/make_norm_golden.py): the reference's gates, and north_star's relative bars
+    (1e-5 F32; F16 within one F16 ulp).  F16 RMSNorm is the F16-boundary form, which casts the
+    normalised value to F16 before the weight multiplies it, as the upstream module does."""
+    c = upstream_norm_case(name)
+    w = c["w"].astype(np.float32)
+    if c["layer"]:
+        h, y = orc.add_layernorm(c["x"], c["r"], w, c["b"].astype(np.float32), 1e-5)
+    else:
+        h, y = orc.add_rmsnorm(c["x"], c["r"], w, 1e-5, f16_boundary=c["half"])
+    assert np.array_equal(h, c["h"])
+    assert_upstream_gates(y, c["y"], name)
+    if not c["half"]:
+        assert_close(y.astype(np.float64), c["y"].astype(np.float64), 1e-5, name)
+    if name == "rms_f16":
+        assert np.array_equal(y, c["y"])  # every value bit-identical to the upstream module's
 
 
 # --------------------------------------------------------------------------- CFG + Euler
