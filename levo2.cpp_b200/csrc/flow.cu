@@ -16,7 +16,6 @@
 // element stops updating at its first failure, keeping its state after the
 // last step it completed.
 #include <algorithm>
-#include <climits>
 #include <cmath>
 #include <string>
 
