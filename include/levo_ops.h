@@ -500,7 +500,12 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
  * call returns LEVO_OPS_ENONFINITE with the reference's message ("Euler velocity
  * contains a non-finite value" / "Euler state contains a non-finite value").
  * On success *completed_steps = first_step + count.  All batch rows form one
- * solve: they stop together.
+ * solve: they stop together.  Before any step, like the reference
+ * (:71-72,81), it returns LEVO_OPS_ENONFINITE ("Euler noise / in-context
+ * latent / resume state contains a non-finite value") with `state` untouched
+ * when noise (or, without noise, the starting state at first_step 0), the
+ * whole context [batch][row], or the state it resumes from (first_step > 0)
+ * holds a non-finite value.
  * checkpoint: caller-owned device scratch of batch * row F32 (the state before
  * the call, kept to replay the completed steps after a failure); status: a
  * caller-owned device int32 (receives LEVO_EULER_STATUS).  Synchronous: the
@@ -532,7 +537,10 @@ typedef const float *(*levo_velocity_fn)(void *user, const float *state, int64_t
  * the in-context interpolation (:93-101), calls `velocity`, and runs the fused
  * CFG combine + Euler update with the reference's finiteness checks
  * (:104,106), reading the status back after each step; after the last step it
- * restores the context prefix (:113-114).
+ * restores the context prefix (:113-114).  Before the first step it checks
+ * noise, context (both [frames][latent_dim]) and, when resuming, the state as
+ * the reference does (:71-72,81): LEVO_OPS_ENONFINITE with its message and
+ * `state` untouched.
  * checkpoint (optional device [frames * latent_dim] F32): the state before each
  * step is kept there, so that on a non-finite velocity or state the solve
  * leaves `state` at the reference's checkpoint (:107-110) and returns

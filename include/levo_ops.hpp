@@ -187,7 +187,8 @@ void solve_flow_euler(const euler_device_input &in, int64_t steps, bool cfg, flo
     std::string msg = levo_ops_last_error();
     const std::string own = "levo_flow_euler_solve_f32: ";
     if (msg.rfind(own, 0) == 0) msg.erase(0, own.size());
-    if (rc == LEVO_OPS_ENONFINITE) msg.erase(msg.find(" (step"));  // the reference names no step
+    const std::size_t step_note = msg.find(" (step");  // the reference names no step
+    if (rc == LEVO_OPS_ENONFINITE && step_note != std::string::npos) msg.erase(step_note);
     throw std::runtime_error(std::string(detail::kFlow) + msg);
 }
 

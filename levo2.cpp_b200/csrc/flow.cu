@@ -342,6 +342,74 @@ int64_t grid_for(int64_t items) {
         1, std::min<int64_t>((items + kThreads - 1) / kThreads, static_cast<int64_t>(sm_count()) * 16));
 }
 
+// Argument checks of the multi-step form, in the reference's order
+// (src/levo-flow-renderer.cpp:63-70), shared by the multi-step call and the solve.
+int multi_args_error(const std::string &w, const float *state, const float *noise, const float *context,
+                     const float *uncond, const float *cond, int64_t batch, int64_t row, int64_t prefix,
+                     int64_t first_step, int64_t count, int64_t steps, int32_t cfg, float guidance,
+                     float sigma_min, const int32_t *status) {
+    if (state == nullptr || (count > 0 && (uncond == nullptr || (cfg && cond == nullptr))))
+        return set_error(LEVO_OPS_EINVAL, w + ": required pointer is null");
+    if (prefix > 0 && (noise == nullptr || context == nullptr))
+        return set_error(LEVO_OPS_EINVAL, w + ": in-context tensors are null");
+    if (batch <= 0 || row <= 0)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler state dimensions must be positive");
+    if (steps <= 0)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler step count must be positive");
+    if (prefix < 0 || prefix > row)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler in-context length exceeds frame count");
+    if (first_step < 0 || count < 0 || first_step > steps || count > steps - first_step)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler resume step exceeds total steps");
+    if (steps >= LEVO_EULER_STEP_LIMIT)
+        return set_error(LEVO_OPS_EUNSUPPORTED, w + ": Euler step count above the status limit");
+    if (!std::isfinite(sigma_min) || sigma_min <= 0.f)
+        return set_error(LEVO_OPS_EINVAL, w + ": Euler sigma_min must be finite and positive");
+    if (cfg && !std::isfinite(guidance))
+        return set_error(LEVO_OPS_EINVAL, w + ": CFG guidance scale must be finite");
+    const void *ptrs[6] = {state, noise, context, uncond, cond, status};
+    for (const void *p : ptrs)
+        if (p && !aligned_to(p, 4))
+            return set_error(LEVO_OPS_EINVAL, w + ": pointer is not 4-byte aligned");
+    return LEVO_OPS_OK;
+}
+
+// solve_flow_euler's finiteness checks of its inputs before the first step
+// (src/levo-flow-renderer.cpp:71-72,81): bit 0 the noise, bit 1 the in-context
+// latent, bit 2 the resume state (any of them may be null).  One warp-wide OR,
+// one atomic per warp.
+__global__ void euler_inputs_kernel(const float *noise, const float *ctx, const float *resume, int64_t n,
+                                    int32_t *bits_out) {
+    int bits = 0;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        if (noise != nullptr && !isfinite(noise[i])) bits |= 1;
+        if (ctx != nullptr && !isfinite(ctx[i])) bits |= 2;
+        if (resume != nullptr && !isfinite(resume[i])) bits |= 4;
+    }
+    bits = static_cast<int>(__reduce_or_sync(0xffffffffu, static_cast<unsigned>(bits)));
+    if ((threadIdx.x & 31) == 0 && bits != 0) atomicOr(bits_out, bits);
+}
+
+// Runs those checks on `stream` with `scratch` (one device int32) and returns
+// the reference's error for the first input it names, or LEVO_OPS_OK.
+int euler_inputs_error(const std::string &w, const float *noise, const float *ctx, const float *resume, int64_t n,
+                       int32_t *scratch, cudaStream_t stream) {
+    cudaError_t err = cudaMemsetAsync(scratch, 0, sizeof(int32_t), stream);
+    if (err == cudaSuccess) {
+        euler_inputs_kernel<<<static_cast<unsigned>(grid_for(n)), kThreads, 0, stream>>>(noise, ctx, resume, n,
+                                                                                          scratch);
+        err = cudaGetLastError();
+    }
+    int32_t bits = 0;
+    if (err == cudaSuccess) err = cudaMemcpyAsync(&bits, scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return set_error(LEVO_OPS_ECUDA, w + ": " + cudaGetErrorString(err));
+    if (bits & 1) return set_error(LEVO_OPS_ENONFINITE, w + ": Euler noise contains a non-finite value");
+    if (bits & 2) return set_error(LEVO_OPS_ENONFINITE, w + ": Euler in-context latent contains a non-finite value");
+    if (bits & 4) return set_error(LEVO_OPS_ENONFINITE, w + ": Euler resume state contains a non-finite value");
+    return LEVO_OPS_OK;
+}
+
 }  // namespace
 }  // namespace levo
 
@@ -423,30 +491,9 @@ LEVO_OPS_API int levo_cfg_euler_multi_f32(float *state, const float *noise, cons
                                           levo_stream_t stream) {
     using namespace levo;
     clear_error();
-    if (state == nullptr || (count > 0 && (uncond == nullptr || (cfg && cond == nullptr))))
-        return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: required pointer is null");
-    if (prefix > 0 && (noise == nullptr || context == nullptr))
-        return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: in-context tensors are null");
-    if (batch <= 0 || row <= 0)
-        return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: Euler state dimensions must be positive");
-    if (steps <= 0)
-        return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: Euler step count must be positive");
-    if (prefix < 0 || prefix > row)
-        return set_error(LEVO_OPS_EINVAL,
-                         "levo_cfg_euler_multi_f32: Euler in-context length exceeds frame count");
-    if (first_step < 0 || count < 0 || first_step > steps || count > steps - first_step)
-        return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: Euler resume step exceeds total steps");
-    if (steps >= LEVO_EULER_STEP_LIMIT)
-        return set_error(LEVO_OPS_EUNSUPPORTED, "levo_cfg_euler_multi_f32: Euler step count above the status limit");
-    if (!std::isfinite(sigma_min) || sigma_min <= 0.f)
-        return set_error(LEVO_OPS_EINVAL,
-                         "levo_cfg_euler_multi_f32: Euler sigma_min must be finite and positive");
-    if (cfg && !std::isfinite(guidance))
-        return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: CFG guidance scale must be finite");
-    const void *ptrs[6] = {state, noise, context, uncond, cond, status};
-    for (const void *p : ptrs)
-        if (p && !aligned_to(p, 4))
-            return set_error(LEVO_OPS_EINVAL, "levo_cfg_euler_multi_f32: pointer is not 4-byte aligned");
+    const int rc = multi_args_error("levo_cfg_euler_multi_f32", state, noise, context, uncond, cond, batch, row,
+                                    prefix, first_step, count, steps, cfg, guidance, sigma_min, status);
+    if (rc != LEVO_OPS_OK) return rc;
     const MultiArgs a{state, noise, context, uncond, cond, batch, row, prefix, first_step,
                       count, steps, cfg ? 1 : 0, guidance, sigma_min, status};
     const int64_t n = batch * row;
@@ -483,13 +530,22 @@ LEVO_OPS_API int levo_cfg_euler_solve_f32(float *state, const float *noise, cons
         return set_error(LEVO_OPS_EINVAL, std::string(w) + ": Euler state dimensions must be positive");
     *completed_steps = first_step;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int rc = multi_args_error(w, state, noise, context, uncond, cond, batch, row, prefix, first_step, count, steps,
+                              cfg, guidance, sigma_min, status);
+    if (rc != LEVO_OPS_OK) return rc;
+    // The reference checks its noise, in-context latent and resume state before any step
+    // (src/levo-flow-renderer.cpp:71-72,81).  Without a noise tensor (no in-context prefix) the
+    // state the solve starts from is the noise.
+    rc = euler_inputs_error(w, noise != nullptr ? noise : (first_step == 0 ? state : nullptr), context,
+                            first_step > 0 ? state : nullptr, batch * row, status, s);
+    if (rc != LEVO_OPS_OK) return rc;
     const size_t bytes = static_cast<size_t>(batch * row) * sizeof(float);
     // the checkpoint of the call's start, then the fused steps
     cudaError_t err = cudaMemcpyAsync(checkpoint, state, bytes, cudaMemcpyDeviceToDevice, s);
     if (err == cudaSuccess) err = cudaMemsetAsync(status, 0, sizeof(int32_t), s);
     if (err != cudaSuccess) return set_error(LEVO_OPS_ECUDA, std::string(w) + ": " + cudaGetErrorString(err));
-    int rc = levo_cfg_euler_multi_f32(state, noise, context, uncond, cond, batch, row, prefix, first_step, count,
-                                      steps, cfg, guidance, sigma_min, status, stream);
+    rc = levo_cfg_euler_multi_f32(state, noise, context, uncond, cond, batch, row, prefix, first_step, count,
+                                  steps, cfg, guidance, sigma_min, status, stream);
     if (rc != LEVO_OPS_OK) {
         cudaStreamSynchronize(s);
         return rc;
@@ -556,6 +612,12 @@ LEVO_OPS_API int levo_flow_euler_solve_f32(float *state, const float *noise, con
     const int64_t n = frames * latent_dim;
     const int64_t prefix = incontext_frames * latent_dim;
     const size_t bytes = static_cast<size_t>(n) * sizeof(float);
+    if (!aligned_to(state, 4) || !aligned_to(noise, 4) || !aligned_to(context, 4) || !aligned_to(status, 4) ||
+        (checkpoint != nullptr && !aligned_to(checkpoint, 4)))
+        return set_error(LEVO_OPS_EINVAL, w + ": pointer is not 4-byte aligned");
+    // the reference's finiteness checks of its inputs before any step (:71-72,81)
+    int rc = euler_inputs_error(w, noise, context, first_step > 0 ? state : nullptr, n, status, s);
+    if (rc != LEVO_OPS_OK) return rc;
     const float dt = 1.0f / static_cast<float>(steps);
     auto cuda_error = [&](cudaError_t err) {
         return set_error(LEVO_OPS_ECUDA, w + ": " + cudaGetErrorString(err));
@@ -569,7 +631,7 @@ LEVO_OPS_API int levo_flow_euler_solve_f32(float *state, const float *noise, con
         if (checkpoint != nullptr) err = cudaMemcpyAsync(checkpoint, state, bytes, cudaMemcpyDeviceToDevice, s);
         if (err == cudaSuccess) err = cudaMemsetAsync(status, 0, sizeof(int32_t), s);
         if (err != cudaSuccess) return cuda_error(err);
-        int rc = LEVO_OPS_OK;
+        rc = LEVO_OPS_OK;
         if (prefix > 0)
             rc = levo_flow_incontext_f32(state, noise, context, 1, n, prefix, step, steps, sigma_min, stream);
         if (rc != LEVO_OPS_OK) return rc;
@@ -599,7 +661,7 @@ LEVO_OPS_API int levo_flow_euler_solve_f32(float *state, const float *noise, con
         *completed_steps = step + 1;
     }
     // final context restore (src/levo-flow-renderer.cpp:113-114): a zero-step multi-step call
-    int rc = levo_cfg_euler_multi_f32(state, noise, context, nullptr, nullptr, 1, n, prefix, steps, 0, steps, 0,
+    rc = levo_cfg_euler_multi_f32(state, noise, context, nullptr, nullptr, 1, n, prefix, steps, 0, steps, 0,
                                       1.0f, sigma_min, nullptr, stream);
     if (rc != LEVO_OPS_OK) return rc;
     const cudaError_t err = cudaStreamSynchronize(s);

@@ -140,6 +140,29 @@ int main() {
     for (int i = 0; i < 6; ++i) CHECK(std::fabs(resumed[i] - ck[i]) < 1e-6F);
     CHECK(to_host(dckpt, 6) == resumed);
     (void)after_step0;
+    // Non-finite noise is rejected before any step (src/levo-flow-renderer.cpp:71), state untouched.
+    std::vector<float> bad_noise = noise;
+    bad_noise[4] = NAN;
+    float *dnoise_bad = to_device(bad_noise);
+    float *dstate3 = to_device(bad_noise);
+    euler_device_input in3{dstate3, dnoise_bad, dctx, 3, 2, 1, 0.1F};
+    int calls = 0;
+    thrown = false;
+    try {
+        solve_flow_euler(
+            in3, 2, false, 1.0F,
+            [&](const float *, int64_t) {
+                ++calls;
+                return static_cast<const float *>(dones);
+            },
+            [] { return false; }, dstatus);
+    } catch (const std::runtime_error &e) {
+        thrown = std::string(e.what()) == "LeVo Flow renderer: Euler noise contains a non-finite value";
+    }
+    CHECK(thrown);
+    CHECK(calls == 0);
+    const std::vector<float> untouched = to_host(dstate3, 6);
+    CHECK(std::isnan(untouched[4]) && untouched[0] == bad_noise[0] && untouched[5] == bad_noise[5]);
 
     // Norm errors carry the prefixes of the reference's LM and Flow estimator (std::runtime_error).
     thrown = false;

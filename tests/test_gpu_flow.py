@@ -191,6 +191,72 @@ def test_solve_stops_at_the_reference_checkpoint(ops, orc, dev, case, layout, wh
 
 
 @pytest.mark.skipif("not __import__('levo_oracle').ref_available()")
+@pytest.mark.parametrize("which", ["noise", "in-context latent", "resume state"])
+@pytest.mark.parametrize("solve", ["fused", "per-step"])
+def test_solve_rejects_nonfinite_inputs_before_any_step(ops, orc, dev, which, solve):
+    """solve_flow_euler checks its noise, in-context latent and resume state before the first step
+    (src/levo-flow-renderer.cpp:71-72,81) and throws without stepping.  Both solve entry points do the
+    same: the reference's message, completed_steps at the start, the state untouched.  The non-finite
+    context value sits outside the in-context prefix, which the steps never read: only the up-front
+    check sees it."""
+    frames, dim, steps, pf = 7, 5, 9, 2
+    n = frames * dim
+    rng = np.random.default_rng(23)
+    noise, ctx = rng.standard_normal((2, n)).astype(np.float32)
+    vu, vc = rng.standard_normal((2, steps, n)).astype(np.float32)
+    first = 3 if which == "resume state" else 0
+    start = noise.copy()
+    if which == "noise":
+        noise[n - 2] = np.nan
+        start = noise.copy()
+    elif which == "in-context latent":
+        ctx[n - 2] = np.inf
+    else:
+        start = rng.standard_normal(n).astype(np.float32)
+        start[n - 2] = np.nan
+    message = f"Euler {which} contains a non-finite value"
+    with pytest.raises(ValueError, match=message):
+        orc.ref_solve_flow_euler(noise, ctx, frames, dim, pf, 1e-4, steps, vu, vc, guidance=1.5,
+                                 resume_step=first if first else -1, resume_state=start if first else None)
+    st = T(start, dev)
+    with pytest.raises(ops.LevoNonFinite, match=message) as err:
+        if solve == "fused":
+            ops.cfg_euler_solve_t(st, T(noise, dev), T(ctx, dev), T(vu[first:], dev), T(vc[first:], dev), batch=1,
+                                  prefix=pf * dim, first_step=first, count=steps - first, steps=steps)
+        else:
+            vel = T(np.stack([vu, vc], axis=1), dev)  # [steps][2][n]
+            ops.flow_euler_solve_t(st, T(noise, dev), T(ctx, dev), frames=frames, latent_dim=dim,
+                                   incontext_frames=pf, steps=steps, first_step=first,
+                                   velocity=lambda _s, k, _t: vel[k])
+    assert err.value.completed_steps == first
+    assert np.array_equal(st.cpu().numpy(), start, equal_nan=True)
+
+
+@pytest.mark.skipif("not __import__('levo_oracle').ref_available()")
+@pytest.mark.parametrize("layout", [(252, 64, 70), (7, 5, 9)])
+def test_solve_velocity_failure_wins_a_tie_with_a_state_failure(ops, orc, dev, layout):
+    """At one step, a non-finite velocity in one element and a state overflow in another: the reference
+    checks the whole velocity first (src/levo-flow-renderer.cpp:104), so the velocity failure is the one
+    reported."""
+    frames, dim, steps = layout
+    prefix_frames = 1
+    fail_step = steps - 3
+    state_element, velocity_element = prefix_frames * dim + 5, prefix_frames * dim + 11
+    noise, ctx, vu, vc = _failing_case("state", frames, dim, steps, prefix_frames, fail_step, state_element)
+    vc[fail_step, velocity_element] = np.nan
+    status, want, done, _ = orc.ref_solve_flow_euler(noise, ctx, frames, dim, prefix_frames, 1e-4, steps, vu, vc,
+                                                     guidance=1.5)
+    assert status == 2 and done == fail_step and "velocity" in orc.ref_last_message()
+    st = T(noise, dev)
+    with pytest.raises(ops.LevoNonFinite) as err:
+        ops.cfg_euler_solve_t(st, T(noise, dev), T(ctx, dev), T(vu, dev), T(vc, dev), batch=1,
+                              prefix=prefix_frames * dim, first_step=0, count=steps, steps=steps)
+    assert err.value.completed_steps == fail_step
+    assert f"Euler velocity contains a non-finite value (step {fail_step})" in str(err.value)
+    assert np.array_equal(st.cpu().numpy(), want)
+
+
+@pytest.mark.skipif("not __import__('levo_oracle').ref_available()")
 def test_solve_resumed_after_a_pause_stops_at_the_same_checkpoint(ops, orc, dev):
     frames, dim, steps, prefix_frames, fail_step = 252, 64, 12, 1, 9
     noise, ctx, vu, vc = _failing_case("velocity", frames, dim, steps, prefix_frames, fail_step, 100)
