@@ -616,11 +616,22 @@ LEVO_OPS_API int levo_greedy_tokens_f32(const float *logits, int64_t rows, int64
  * Requires 2 <= overlap <= hop and hop + overlap <= window (or overlap == 0), as
  * the reference's 750 / 250 / 1000-frame schedule satisfies.  Bit-identical to
  * the reference (same F32 expression order).
+ * status (optional device int32, zeroed by the caller): the reference rejects
+ * a decoded window holding a non-finite sample (require_finite_audio, :159-160:
+ * "decoded left / right channel contains non-finite samples", windows in
+ * order, left before right).  Every sample of every window is checked, and the
+ * first failing pair is recorded as LEVO_ASSEMBLE_STATUS(window * channels +
+ * channel) (0: all finite; the output is then not the reference's, which
+ * throws).  n_windows * channels must stay below LEVO_ASSEMBLE_STATUS_LIMIT.
  */
+#define LEVO_ASSEMBLE_STATUS_LIMIT 1073741824 /* 2^30 */
+#define LEVO_ASSEMBLE_STATUS(pair) (LEVO_ASSEMBLE_STATUS_LIMIT - (pair))
+#define LEVO_ASSEMBLE_STATUS_PAIR(word) (LEVO_ASSEMBLE_STATUS_LIMIT - (word))
 LEVO_OPS_API int levo_assemble_windows_f32(const float *windows, int64_t n_windows, int64_t channels,
                                            int64_t window_samples, int64_t hop_samples,
                                            int64_t overlap_samples, int64_t target_samples,
-                                           float *out, int32_t interleaved, levo_stream_t stream);
+                                           float *out, int32_t interleaved, int32_t *status,
+                                           levo_stream_t stream);
 
 #ifdef __cplusplus
 }

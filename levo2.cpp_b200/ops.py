@@ -44,6 +44,11 @@ class LevoNonFinite(LevoOpsError):
     completed_steps: Optional[int] = None
 
 
+class LevoNonFiniteAudio(LevoNonFinite, ValueError):
+    """A decoded window given to the window assembly holds a non-finite sample: the reference's
+    assemble_renderer_audio throws std::invalid_argument (src/levo-renderer-pattern.cpp:25-28,159-160)."""
+
+
 class Topology(ctypes.Structure):
     _fields_ = [
         ("latent_dim", ctypes.c_int32),
@@ -162,7 +167,7 @@ SIGNATURES = {
     "levo_greedy_tokens_f32": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P, _P, _P]),
     "levo_latent_to_vae_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
     "levo_latent_normalize_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
-    "levo_assemble_windows_f32": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P]),
+    "levo_assemble_windows_f32": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P, _P]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -460,9 +465,14 @@ def flow_euler_solve_t(state, noise, context, *, frames, latent_dim, incontext_f
     return done.value
 
 
+ASSEMBLE_STATUS_LIMIT = 1 << 30
+
+
 def assemble_windows_t(windows, hop_samples: int, overlap_samples: int, target_samples: int, interleaved=False,
-                       out=None):
-    """Crossfade-assemble decoded windows [W, C, S] into [C, target] (or [target, C] interleaved)."""
+                       out=None, check_finite=True):
+    """Crossfade-assemble decoded windows [W, C, S] into [C, target] (or [target, C] interleaved).
+    With check_finite (the reference's require_finite_audio) a non-finite sample in any window raises
+    LevoNonFinite with the reference's message for the first (window, channel), after a synchronize."""
     import torch
 
     _require_cuda(windows, out)
@@ -470,8 +480,17 @@ def assemble_windows_t(windows, hop_samples: int, overlap_samples: int, target_s
     if out is None:
         shape = (target_samples, c) if interleaved else (c, target_samples)
         out = torch.empty(shape, dtype=torch.float32, device=windows.device)
+    status = torch.zeros(1, dtype=torch.int32, device=windows.device) if check_finite else None
     check(lib().levo_assemble_windows_f32(_ptr(windows), w, c, s, hop_samples, overlap_samples, target_samples,
-                                          _ptr(out), 1 if interleaved else 0, _stream(windows.device)))
+                                          _ptr(out), 1 if interleaved else 0, _ptr(status),
+                                          _stream(windows.device)))
+    word = int(status.item()) if status is not None else 0
+    if word:
+        pair = ASSEMBLE_STATUS_LIMIT - word
+        k, ch = divmod(pair, c)
+        name = ("left", "right")[ch] if c == 2 else f"{ch}"
+        raise LevoNonFiniteAudio(ENONFINITE, f"levo_assemble_windows_f32: decoded {name} channel contains "
+                                             f"non-finite samples (window {k})")
     return out
 
 

@@ -57,3 +57,54 @@ def test_assembly_rejects_chained_overlaps(ops, dev):
         ops.assemble_windows_t(w, 4, 6, 12)
     with pytest.raises(ValueError, match="target crop"):
         ops.assemble_windows_t(w, 5, 5, 16)
+
+
+# (window, channel, sample) plants; the reference reports the first window in order, left before right
+PLANTS = {
+    "window 0 right, start": [(0, 1, 5)],
+    "window 1 left, crossfaded head": [(1, 0, 17)],
+    "window 0 left, tail read as the next window's overlap": [(0, 0, HOP + 3)],
+    "later window listed first": [(2, 0, 0), (1, 1, WIN - 1)],
+    "last window, past the crop": [(-1, 0, WIN - 1)],
+}
+
+
+@pytest.mark.parametrize("plant", list(PLANTS))
+@pytest.mark.parametrize("bad", [np.nan, np.inf])
+def test_assembly_rejects_nonfinite_like_the_reference(ops, orc, dev, plant, bad):
+    """assemble_renderer_audio rejects a decoded window holding a non-finite sample with
+    std::invalid_argument naming the channel of the first failing window (src/levo-renderer-pattern.cpp:
+    25-28,159-160); the CUDA path raises a ValueError with the same text for the same window and channel."""
+    source_frames = 2300  # 3 windows; the crop ends inside the last one
+    n = 3
+    target = source_frames * 1920
+    rng = np.random.default_rng(7)
+    w = rng.standard_normal((n, 2, WIN)).astype(np.float32)
+    for k, c, s in PLANTS[plant]:
+        w[k, c, s] = bad
+    k_first, c_first = min((k % n, c) for k, c, _ in PLANTS[plant])
+    side = ("left", "right")[c_first]
+    if orc.ref_available():
+        assert len(orc.ref_make_renderer_schedule(source_frames)["windows"]) == n
+        with pytest.raises(ValueError, match=f"decoded {side} channel contains non-finite samples"):
+            orc.ref_assemble_renderer_audio(source_frames, w[:, 0], w[:, 1])
+    with pytest.raises(ValueError, match=f"decoded {side} channel contains non-finite samples \\(window {k_first}\\)"):
+        ops.assemble_windows_t(torch.from_numpy(w).to(dev), HOP, OV, target)
+
+
+@pytest.mark.parametrize("k,s", [(0, 18), (1, 17), (2, 19), (2, 5)])
+def test_assembly_checks_samples_no_output_reads(ops, dev, k, s):
+    """3 windows of 20 samples, hop 12, overlap 5, crop at 43: samples 17..19 of windows 0 and 1 feed no
+    output (hop + overlap = 17), nor does sample 19 of the last window (it would land at 43); sample 5
+    of the last window is read.  Every sample is still checked, as the reference checks whole windows."""
+    w = np.zeros((3, 2, 20), np.float32)
+    w[k, 1, s] = np.nan
+    with pytest.raises(ValueError, match=f"decoded right channel contains non-finite samples \\(window {k}\\)"):
+        ops.assemble_windows_t(torch.from_numpy(w).to(dev), 12, 5, 43)
+
+
+def test_assembly_without_the_check_runs_through(ops, dev):
+    w = torch.zeros((2, 2, 10), device=dev)
+    w[1, 0, 9] = float("nan")
+    out = ops.assemble_windows_t(w, 5, 5, 15, check_finite=False)
+    assert torch.isnan(out[0, 14]).item()
