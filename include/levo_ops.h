@@ -568,16 +568,23 @@ LEVO_OPS_API int levo_flow_euler_solve_f32(float *state, const float *noise, con
  * renderer's frame-major [frames][dim] window becomes the VAE's channel-major
  * [dim][frames] input in one pass.  mean and stddev both NULL: transpose only.
  * Not in place.  Bit-identical to the reference (mul then add, no FMA).
+ * status (optional device int32, zeroed by the caller): bit 0 set when an
+ * input value is non-finite, where the reference throws "normalized latent
+ * contains a non-finite value" (:128).
  */
 LEVO_OPS_API int levo_latent_to_vae_f32(const float *frame_major, const float *mean, const float *stddev,
                                         int64_t frames, int64_t dim, float *channel_major,
-                                        levo_stream_t stream);
+                                        int32_t *status, levo_stream_t stream);
 /*
  * normalized[f][c] = (raw[f][c] - mean[c]) / stddev[c], frame-major
  * (normalize_latents, src/levo-flow-conditioning.cpp:113-123).  May run in place.
+ * status (optional device int32, zeroed by the caller): bit 0 set when a raw
+ * value is non-finite, where the reference throws "raw latent contains a
+ * non-finite value" (:116).
  */
 LEVO_OPS_API int levo_latent_normalize_f32(const float *raw, const float *mean, const float *stddev,
-                                           int64_t frames, int64_t dim, float *normalized, levo_stream_t stream);
+                                           int64_t frames, int64_t dim, float *normalized, int32_t *status,
+                                           levo_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* next (f3)  greedy next-token selection over LeLM logits                    */

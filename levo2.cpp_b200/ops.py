@@ -165,8 +165,8 @@ SIGNATURES = {
     "levo_gated_layernorm_modulate_f32": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _F, _P]),
     "levo_vae_decode_noalloc_f32": (_INT, [ctypes.POINTER(Topology), _P, _P, _I64, _P, CONV_FN, _P, _U32, _P]),
     "levo_greedy_tokens_f32": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _F, _I64, _P, _I64, _P, _P, _P]),
-    "levo_latent_to_vae_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
-    "levo_latent_normalize_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
+    "levo_latent_to_vae_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P, _P]),
+    "levo_latent_normalize_f32": (_INT, [_P, _P, _P, _I64, _I64, _P, _P, _P]),
     "levo_assemble_windows_f32": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P, _P]),
 }
 
@@ -508,26 +508,39 @@ def greedy_tokens_t(logits, recent=None, penalty=1.0, penalty_limit=0, ignore=No
     return out
 
 
-def latent_to_vae_t(frame_major, mean=None, stddev=None, out=None):
-    """[frames, dim] frame-major (normalised) latent -> [dim, frames] de-normalised VAE input."""
+def _raise_if_flagged(status, what: str, message: str) -> None:
+    """Reads an optional status word (synchronising) and raises LevoNonFinite when bit 0 is set."""
+    if status is not None and int(status.item()) & 1:
+        raise LevoNonFinite(ENONFINITE, f"{what}: {message}")
+
+
+def latent_to_vae_t(frame_major, mean=None, stddev=None, out=None, check_finite=True):
+    """[frames, dim] frame-major (normalised) latent -> [dim, frames] de-normalised VAE input.  With
+    check_finite a non-finite input raises LevoNonFinite, as denormalize_latents throws."""
     import torch
 
     _require_cuda(frame_major, mean, stddev, out)
     frames, dim = frame_major.shape
     out = torch.empty((dim, frames), dtype=torch.float32, device=frame_major.device) if out is None else out
+    status = torch.zeros(1, dtype=torch.int32, device=frame_major.device) if check_finite else None
     check(lib().levo_latent_to_vae_f32(_ptr(frame_major), _ptr(mean), _ptr(stddev), frames, dim, _ptr(out),
-                                       _stream(frame_major.device)))
+                                       _ptr(status), _stream(frame_major.device)))
+    _raise_if_flagged(status, "levo_latent_to_vae_f32", "normalized latent contains a non-finite value")
     return out
 
 
-def latent_normalize_t(raw, mean, stddev, out=None):
+def latent_normalize_t(raw, mean, stddev, out=None, check_finite=True):
+    """(raw - mean) / stddev per channel; with check_finite a non-finite raw value raises LevoNonFinite,
+    as normalize_latents throws."""
     import torch
 
     _require_cuda(raw, mean, stddev, out)
     frames, dim = raw.shape
     out = torch.empty_like(raw) if out is None else out
+    status = torch.zeros(1, dtype=torch.int32, device=raw.device) if check_finite else None
     check(lib().levo_latent_normalize_f32(_ptr(raw), _ptr(mean), _ptr(stddev), frames, dim, _ptr(out),
-                                          _stream(raw.device)))
+                                          _ptr(status), _stream(raw.device)))
+    _raise_if_flagged(status, "levo_latent_normalize_f32", "raw latent contains a non-finite value")
     return out
 
 

@@ -38,3 +38,25 @@ def test_latent_to_vae_rejects_in_place(ops, dev):
     x = torch.zeros((8, 8), device=dev)
     with pytest.raises(ValueError, match="in place"):
         ops.latent_to_vae_t(x, out=x)
+
+
+@pytest.mark.parametrize("bad", [np.nan, np.inf, -np.inf])
+@pytest.mark.parametrize("where", [(0, 0), (749, 63), (400, 17)])
+def test_latent_functions_reject_nonfinite_inputs(ops, dev, bad, where):
+    """normalize_latents / denormalize_latents reject a non-finite input before computing
+    (require_finite, src/levo-flow-conditioning.cpp:42-44,116,128): the same message here; without the
+    check the value just passes through."""
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((750, 64)).astype(np.float32)
+    x[where] = bad
+    mean = rng.standard_normal(64).astype(np.float32)
+    std = rng.uniform(0.5, 2.0, 64).astype(np.float32)
+    T = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+    with pytest.raises(ops.LevoNonFinite, match="raw latent contains a non-finite value"):
+        ops.latent_normalize_t(T(x), T(mean), T(std))
+    with pytest.raises(ops.LevoNonFinite, match="normalized latent contains a non-finite value"):
+        ops.latent_to_vae_t(T(x), T(mean), T(std))
+    got = ops.latent_to_vae_t(T(x), T(mean), T(std), check_finite=False).cpu().numpy()
+    assert not np.isfinite(got[where[1], where[0]])
+    finite = ops.latent_to_vae_t(T(np.nan_to_num(x, posinf=0.0, neginf=0.0)), T(mean), T(std))
+    assert torch.isfinite(finite).all().item()
