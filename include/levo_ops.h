@@ -600,7 +600,8 @@ LEVO_OPS_API int levo_latent_normalize_f32(const float *raw, const float *mean, 
  *   2. row 0 only: ids in ignore[0..n_ignore) become -inf (:146-148);
  *   3. tokens_out[row] = index of the first maximum (std::max_element).
  * Bit-exact with the reference.  recent may be NULL.  status (optional device
- * int32): bit 1 set when a logit is NaN (the reference throws).  vocab <= 131072.
+ * int32, zeroed by the caller): bit 0 (value 1) set when a logit is NaN, where
+ * the reference throws "logits contain NaN" (:81).  vocab <= 131072.
  */
 LEVO_OPS_API int levo_greedy_tokens_f32(const float *logits, int64_t rows, int64_t vocab, int64_t ld,
                                         const int64_t *recent, int64_t recent_len, float penalty,

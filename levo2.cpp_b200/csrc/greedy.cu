@@ -7,8 +7,8 @@
 //   2. on the first stream only, ignored token ids become -inf (:146-148);
 //   3. the result is the index of the FIRST maximum (std::max_element, :93-95);
 //      top-k filtering never removes the maximum, so greedy selection does not
-//      depend on it.  A NaN logit is an error in the reference (:79); here it
-//      sets bit 1 of the optional status word.
+//      depend on it.  A NaN logit is an error in the reference (:81); here it
+//      sets bit 0 (value 1) of the optional status word.
 // One CTA per stream row: the recent / ignored ids are marked in shared-memory
 // bitmaps, the row is scanned once with coalesced loads, and (value, index)
 // pairs are reduced with a first-index tie break, so the result is exact.
