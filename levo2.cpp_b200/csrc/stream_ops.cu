@@ -73,11 +73,15 @@ __device__ __forceinline__ ChannelParams channel_params(const StreamArgs &a, con
             p.beta = smem[a.rows + c];
         }
         if (a.has_bias) p.bias = smem[2 * a.rows + c];
+    } else if constexpr (SNAKE) {
+        // The three loads go out together, ahead of the exponentials: a bias load
+        // behind the has_bias branch cannot be hoisted (the pointer may be null)
+        // and would start one L2 round trip later in every chunk.
+        const float bias = load_param(a.has_bias ? a.bias : a.alog, c, a.pdtype);
+        p.alpha = snake_alpha_param(a.alog, c, a.pdtype);
+        p.beta = snake_inv_beta_param(a.blog, c, a.pdtype);
+        if (a.has_bias) p.bias = bias;
     } else {
-        if (SNAKE) {
-            p.alpha = snake_alpha_param(a.alog, c, a.pdtype);
-            p.beta = snake_inv_beta_param(a.blog, c, a.pdtype);
-        }
         if (a.has_bias) p.bias = load_param(a.bias, c, a.pdtype);
     }
     return p;
