@@ -218,6 +218,9 @@ struct levo_vae_chain {
     int64_t max_elems = 0;
     void *params = nullptr;       // packed parameters, F32 or F16 (pdtype)
     int pdtype = LEVO_DTYPE_F32;
+    // dtype the fused units read the parameters with: an F32 chain holds every
+    // SnakeBeta layer prepared (alpha, 1/beta) and reads LEVO_DTYPE_SNAKE_PREPARED
+    int unit_pdtype = LEVO_DTYPE_F32;
     float *X = nullptr;
     float *A = nullptr;
     float *B = nullptr;
@@ -384,7 +387,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
         u.y_out = cur;
         u.channels = t.entry_width;
         u.time = frames;
-        u.param_dtype = c->pdtype;
+        u.param_dtype = c->unit_pdtype;
         rc = run_unit(c, timing, LEVO_KCLASS_ENTRY, u, s);
         if (rc != LEVO_OPS_OK) return rc;
     }
@@ -424,7 +427,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
             u.y_out = cur;
             u.channels = cout;
             u.time = lout;
-            u.param_dtype = c->pdtype;
+            u.param_dtype = c->unit_pdtype;
             rc = run_unit(c, timing, LEVO_KCLASS_UPSAMPLE, u, s);
             if (rc != LEVO_OPS_OK) return rc;
         }
@@ -455,7 +458,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
                 u.y_out = cur;
                 u.channels = cout;
                 u.time = lout;
-                u.param_dtype = c->pdtype;
+                u.param_dtype = c->unit_pdtype;
                 rc = run_unit(c, timing, LEVO_KCLASS_POST, u, s);
                 if (rc != LEVO_OPS_OK) return rc;
             }
@@ -488,7 +491,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
                 u.y_out = cur;
                 u.channels = cout;
                 u.time = lout;
-                u.param_dtype = c->pdtype;
+                u.param_dtype = c->unit_pdtype;
                 rc = run_unit(c, timing, LEVO_KCLASS_RESIDUAL, u, s);
                 if (rc != LEVO_OPS_OK) return rc;
             }
@@ -529,7 +532,7 @@ int decode_one(levo_vae_chain *c, const float *latent, int64_t frames, float *au
         u.y_out = audio_out;
         u.channels = t.audio_channels;
         u.time = len;
-        u.param_dtype = c->pdtype;
+        u.param_dtype = c->unit_pdtype;
         u.flags = LEVO_FUSED_TANH;
         rc = run_unit(c, timing, LEVO_KCLASS_EPILOGUE, u, s);
         if (rc != LEVO_OPS_OK) return rc;
@@ -629,6 +632,48 @@ LEVO_OPS_API int levo_conv_standin_f32(const float *in, int64_t in_channels, int
     return check_launch("levo_conv_standin_f32");
 }
 
+// An F32 chain replaces each SnakeBeta layer's (alpha_log, beta_log) by
+// (alpha, 1/beta) once, with the library's own prepare kernel (bit-identical to
+// the exponentials every launch would otherwise take, src/levo-audio-ops.cpp:
+// 146-151): the fused units then start each chunk with three plain loads.  The
+// activation buffer A is the scratch; the work runs and is waited for on the
+// legacy default stream, like the parameter upload before it.
+static int prepare_snake_layers(levo_vae_chain *c) {
+    using namespace levo;
+    const levo_vae_topology &t = c->topo;
+    const Layout &l = c->layout;
+    float *p = static_cast<float *>(c->params);
+    struct Pair {
+        int64_t alpha, beta, n;
+    };
+    std::vector<Pair> pairs;
+    int64_t cin = t.entry_width;
+    for (int s = 0; s < t.n_stages; ++s) {
+        pairs.push_back({l.stage[s].up_alpha, l.stage[s].up_beta, cin});
+        for (int r = 0; r < t.n_residual; ++r) {
+            pairs.push_back({l.stage[s].pre_alpha[r], l.stage[s].pre_beta[r], t.stage_width[s]});
+            pairs.push_back({l.stage[s].post_alpha[r], l.stage[s].post_beta[r], t.stage_width[s]});
+        }
+        cin = t.stage_width[s];
+    }
+    pairs.push_back({l.out_alpha, l.out_beta, cin});
+    for (const Pair &q : pairs) {
+        if (2 * q.n > c->max_elems) return set_error(LEVO_OPS_EINVAL, "levo_vae_chain_create: scratch too small");
+        const int rc = levo_snake_params_prepare(p + q.alpha, p + q.beta, LEVO_DTYPE_F32, q.n, c->A, c->A + q.n,
+                                                 nullptr);
+        if (rc != LEVO_OPS_OK) return rc;
+        const size_t bytes = static_cast<size_t>(q.n) * sizeof(float);
+        cudaError_t err = cudaMemcpyAsync(p + q.alpha, c->A, bytes, cudaMemcpyDeviceToDevice, nullptr);
+        if (err == cudaSuccess)
+            err = cudaMemcpyAsync(p + q.beta, c->A + q.n, bytes, cudaMemcpyDeviceToDevice, nullptr);
+        if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_create: parameter preparation");
+    }
+    const cudaError_t err = cudaStreamSynchronize(nullptr);
+    if (err != cudaSuccess) return cuda_fail(err, "levo_vae_chain_create: parameter preparation");
+    c->unit_pdtype = LEVO_DTYPE_SNAKE_PREPARED;
+    return LEVO_OPS_OK;
+}
+
 static int create_chain(levo_vae_chain **out, const levo_vae_topology *topology, const void *params_host,
                         int pdtype, int64_t max_frames, levo_conv_fn conv, void *conv_user, int device) {
     using namespace levo;
@@ -648,6 +693,7 @@ static int create_chain(levo_vae_chain **out, const levo_vae_topology *topology,
     if (c == nullptr) return set_error(LEVO_OPS_ENOMEM, "levo_vae_chain_create: out of host memory");
     c->device = device;
     c->pdtype = pdtype;
+    c->unit_pdtype = pdtype;
     c->topo = *topology;
     c->layout = make_layout(*topology);
     c->max_frames = max_frames;
@@ -691,6 +737,13 @@ static int create_chain(levo_vae_chain **out, const levo_vae_topology *topology,
         const int rc = cuda_fail(err, "levo_vae_chain_create");
         free_chain(c);
         return rc;
+    }
+    if (pdtype == LEVO_DTYPE_F32) {
+        const int rc = prepare_snake_layers(c);
+        if (rc != LEVO_OPS_OK) {
+            free_chain(c);
+            return rc;
+        }
     }
     *out = c;
     return LEVO_OPS_OK;
