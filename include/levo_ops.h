@@ -214,7 +214,10 @@ typedef struct levo_vae_chain levo_vae_chain;
  * activation workspace for windows of up to `max_frames` latent frames (three
  * [max C*L] F32 buffers plus double-buffered window I/O).  Mirrors
  * vae_decoder::create (src/levo-vae.cpp:168-170) with the graph allocation of
- * decode (src/levo-vae.cpp:242-246) done once up front.
+ * decode (src/levo-vae.cpp:242-246) done once up front.  On the device each
+ * SnakeBeta layer is kept as (alpha, 1/beta), computed once here by
+ * levo_snake_params_prepare (bit-identical to exponentiating the log form in
+ * every launch); the call waits for that work on the legacy default stream.
  */
 LEVO_OPS_API int levo_vae_chain_create(levo_vae_chain **out, const levo_vae_topology *topology,
                                        const float *params_host, int64_t max_frames,
