@@ -37,10 +37,13 @@ __device__ __forceinline__ float block_sum(float s, float *red) {
     return t;
 }
 
-__device__ __forceinline__ float row_scale(const WnArgs &a, int64_t row, float sumsq) {
+// gain = g[row], loaded by the caller before the row's reduction: a load after
+// block_sum's barrier could not be moved above it and would add one memory
+// round trip between the reduction and the stores of every row.
+__device__ __forceinline__ float row_scale(const WnArgs &a, int64_t row, float gain, float sumsq) {
     const float norm = __fsqrt_rn(sumsq);
     if (a.norms && threadIdx.x == 0) a.norms[row] = norm;
-    return __fdiv_rn(a.g[row], norm);
+    return __fdiv_rn(gain, norm);
 }
 
 // VPT > 0: the row is register resident (VPT 8-float vectors per thread).
@@ -50,6 +53,7 @@ __global__ void __launch_bounds__(256) weightnorm_vec_kernel(const WnArgs a) {
     __shared__ float red[32];
     const int64_t nvec = a.cols / 8;
     for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        const float gain = a.g[row];
         const float *vr = a.v + row * a.cols;
         float *wr = a.w + row * a.cols;
         if constexpr (VPT > 0) {
@@ -68,7 +72,7 @@ __global__ void __launch_bounds__(256) weightnorm_vec_kernel(const WnArgs a) {
                     for (int j = 0; j < 8; ++j) s = fmaf(buf[k].v[j], buf[k].v[j], s);
                 }
             }
-            const float scale = row_scale(a, row, block_sum(s, red));
+            const float scale = row_scale(a, row, gain, block_sum(s, red));
 #pragma unroll
             for (int k = 0; k < VPT; ++k) {
                 const int64_t vi = k * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -86,7 +90,7 @@ __global__ void __launch_bounds__(256) weightnorm_vec_kernel(const WnArgs a) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) s = fmaf(b.v[j], b.v[j], s);
             }
-            const float scale = row_scale(a, row, block_sum(s, red));
+            const float scale = row_scale(a, row, gain, block_sum(s, red));
             for (int64_t vi = threadIdx.x; vi < nvec; vi += blockDim.x) {
                 f32x8 b = ld8(vr + vi * 8);
 #pragma unroll
@@ -126,6 +130,7 @@ __global__ void __launch_bounds__(kStagedThreads, 4) weightnorm_staged_kernel(co
     if (row < a.rows) issue(row);
     cp_async_commit();
     for (; row < a.rows; row += gridDim.x) {
+        const float gain = a.g[row];
         cp_async_wait_group<0>();
         __syncthreads();  // the row is in shared memory
         float4 b[CPT];
@@ -148,7 +153,7 @@ __global__ void __launch_bounds__(kStagedThreads, 4) weightnorm_staged_kernel(co
                 s = fmaf(b[k].w, b[k].w, s);
             }
         }
-        const float scale = row_scale(a, row, block_sum(s, red));
+        const float scale = row_scale(a, row, gain, block_sum(s, red));
         float4 *wr = reinterpret_cast<float4 *>(a.w + row * a.cols);
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
@@ -195,11 +200,12 @@ void launch_staged(const WnArgs &a, int cpt, cudaStream_t stream) {
 __global__ void __launch_bounds__(256) weightnorm_scalar_kernel(const WnArgs a) {
     __shared__ float red[32];
     for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        const float gain = a.g[row];
         const float *vr = a.v + row * a.cols;
         float *wr = a.w + row * a.cols;
         float s = 0.f;
         for (int64_t j = threadIdx.x; j < a.cols; j += blockDim.x) s = fmaf(vr[j], vr[j], s);
-        const float scale = row_scale(a, row, block_sum(s, red));
+        const float scale = row_scale(a, row, gain, block_sum(s, red));
         for (int64_t j = threadIdx.x; j < a.cols; j += blockDim.x) wr[j] = __fmul_rn(vr[j], scale);
     }
 }
