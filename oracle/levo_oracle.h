@@ -60,8 +60,9 @@ int oracle_vae_chain_stages_f32(const int32_t *topology, const float *params, co
  * RMSNorm: src/levo-lm.cpp:131-138, src/levo-kv.cpp:153-170.
  * LayerNorm: src/levo-flow-estimator.cpp:106-109.  r / h_out may be NULL.
  * PARITY UNPINNED against the reference itself: its norms are the GGML nodes
- * ggml_rms_norm / ggml_norm, and GGML (the reference's `ggml` submodule, whose
- * commit this tree does not record) is absent.  The restatement follows GGML's
+ * ggml_rms_norm / ggml_norm, and GGML (the reference's `ggml` submodule,
+ * ggml-org/ggml @ 8846b79e66747bb9f68597420e95114c177315ce as
+ * src/levo-vae-model.cpp:132 records it) is absent.  The restatement follows GGML's
  * published CPU algorithm (row statistics accumulated in double, the scale
  * 1/sqrt(stat + eps) in F32, then separate gamma / beta nodes) and is checked
  * against the float64 definitions and against the upstream modules the
