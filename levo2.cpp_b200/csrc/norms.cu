@@ -621,8 +621,12 @@ __device__ __forceinline__ uint4 norm_chunk_out(uint4 hc, const float4 *gs, cons
     return Chunk<T>::pack(h);
 }
 
+// With 6 or more chunks per lane, LayerNorm's gamma and beta and the rows leave
+// room for at most 3 of its CTAs on an SM (dim 1536 F16: 60 KB each), so its
+// register cap can rise to ~85 without costing occupancy: at the 64-register
+// cap of 4 CTAs the compiler's schedule cost ~0.25 us at config 1.
 template <typename T, bool LAYER, bool BOUND, int CPL>
-__global__ void __launch_bounds__(kRegsWarps * 32, 4) add_norm_regs_kernel(const NormArgs a) {
+__global__ void __launch_bounds__(kRegsWarps * 32, (LAYER && CPL >= 6) ? 3 : 4) add_norm_regs_kernel(const NormArgs a) {
     extern __shared__ uint4 sbuf[];
     constexpr int N = Chunk<T>::kN;
     const int warp = threadIdx.x >> 5;
