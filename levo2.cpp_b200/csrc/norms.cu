@@ -621,12 +621,19 @@ __device__ __forceinline__ uint4 norm_chunk_out(uint4 hc, const float4 *gs, cons
     return Chunk<T>::pack(h);
 }
 
-// With 6 or more chunks per lane, LayerNorm's gamma and beta and the rows leave
-// room for at most 3 of its CTAs on an SM (dim 1536 F16: 60 KB each), so its
-// register cap can rise to ~85 without costing occupancy: at the 64-register
-// cap of 4 CTAs the compiler's schedule cost ~0.25 us at config 1.
+// Shared memory of a CTA whose rows fill its CPL chunks per lane: two rows (x, r)
+// per warp plus gamma (and beta) in F32.  When 4 such CTAs do not fit an SM
+// (228 KB, 1 KB reserved per CTA), the register cap is that of 3 CTAs (~85)
+// instead of 64: at dim 1536 F16 LayerNorm (60 KB) the 64-register schedule
+// cost ~0.25 us at config 1, and RMSNorm / LayerNorm with 8 chunks spilled.
+template <typename T, bool LAYER, int CPL>
+constexpr int regs_min_ctas() {
+    constexpr int smem = kRegsWarps * 2 * CPL * 32 * 16 + (LAYER ? 2 : 1) * CPL * 32 * Chunk<T>::kN * 4;
+    return 4 * (smem + 1024) <= 228 * 1024 ? 4 : 3;
+}
+
 template <typename T, bool LAYER, bool BOUND, int CPL>
-__global__ void __launch_bounds__(kRegsWarps * 32, (LAYER && CPL >= 6) ? 3 : 4) add_norm_regs_kernel(const NormArgs a) {
+__global__ void __launch_bounds__(kRegsWarps * 32, regs_min_ctas<T, LAYER, CPL>()) add_norm_regs_kernel(const NormArgs a) {
     extern __shared__ uint4 sbuf[];
     constexpr int N = Chunk<T>::kN;
     const int warp = threadIdx.x >> 5;
