@@ -30,7 +30,7 @@ def _inputs(rng, rows, dim, dt):
 
 @pytest.mark.parametrize("layer", [False, True])
 @pytest.mark.parametrize("dt", [np.float16, np.float32])
-@pytest.mark.parametrize("dim", [1, 7, 16, 100, 512, 1536, 2048, 2200, 4096])
+@pytest.mark.parametrize("dim", [1, 7, 16, 100, 512, 768, 1024, 1280, 1536, 2048, 2200, 4096])
 def test_add_norm_matches_oracle(ops, orc, dev, layer, dt, dim):
     rng = np.random.default_rng(dim * 3 + layer)
     rows = 37
