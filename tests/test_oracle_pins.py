@@ -359,3 +359,23 @@ def test_latent_layout_and_normalisation_definitions(orc):
     den = orc.latent_to_vae(x, mean, std)
     assert np.array_equal(den, ((x * std).astype(np.float32) + mean).astype(np.float32).T)
     assert np.array_equal(orc.latent_normalize(x, mean, std), ((x - mean).astype(np.float32) / std).astype(np.float32))
+
+
+def test_upstream_norm_fixture_is_what_its_generator_makes():
+    """tests/golden/norms_upstream.npz holds exactly what tests/golden/make_norm_golden.py computes from the
+    upstream modules (skipped where torch or transformers is missing)."""
+    pytest.importorskip("transformers")
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("make_norm_golden", GOLDEN / "make_norm_golden.py")
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    z = np.load(GOLDEN / "norms_upstream.npz")
+    for name, dt, seed in (("rms_f32", np.float32, 11), ("rms_f16", np.float16, 12)):
+        x, r, w, _, y = gen._rms(np.random.default_rng(seed), 8, 1536, dt)
+        for key, val in (("x", x), ("r", r), ("w", w), ("y", y)):
+            assert np.array_equal(z[f"{name}_{key}"], val), (name, key)
+    for name, dt, seed in (("ln_f32", np.float32, 13), ("ln_f16", np.float16, 14)):
+        x, r, w, b, _, y = gen._ln(np.random.default_rng(seed), 4, 2200, dt)
+        for key, val in (("x", x), ("r", r), ("w", w), ("b", b), ("y", y)):
+            assert np.array_equal(z[f"{name}_{key}"], val), (name, key)
