@@ -69,8 +69,8 @@ def parse():
     p.add_argument("--no-tanh", action="store_true")
     p.add_argument("--only-kernels", action="store_true",
                    help="run only the configs 0-2 kernel suite (small; used for ncu captures)")
-    p.add_argument("--kernels", default="snakebeta,norms,weightnorm,euler",
-                   help="comma-separated subset of the kernel suite: snakebeta, norms, weightnorm, euler")
+    p.add_argument("--kernels", default=",".join(KERNEL_FAMILIES),
+                   help="comma-separated subset of the kernel suite: " + ", ".join(KERNEL_FAMILIES))
     return p.parse_args()
 
 
@@ -334,8 +334,12 @@ def input_sets(set_bytes: int) -> int:
     return max(3, -(-int(2.5 * L2_BYTES) // max(set_bytes, 1)))
 
 
-def kernel_suite(ops, dev, peak, steps, warmup, which=("snakebeta", "norms", "weightnorm", "euler")):
-    """Configs 0-2 kernels.  `ms` is the per-launch time of KERNEL_LAUNCHES back-to-back launches,
+KERNEL_FAMILIES = ("snakebeta", "norms", "weightnorm", "euler", "assembly", "latent", "greedy")
+
+
+def kernel_suite(ops, dev, peak, steps, warmup, which=KERNEL_FAMILIES):
+    """Configs 0-2 kernels, and the kernels of the rows next to the path (window assembly, latent
+    hand-off into the VAE, greedy token selection).  `ms` is the per-launch time of KERNEL_LAUNCHES back-to-back launches,
     rotating over input sets larger than L2 in total, captured once into a CUDA graph and replayed
     between one pair of CUDA events (median of `steps` replays): device time, without the host
     cost of each Python-side launch.  `ms_single_launch` is one eager launch after an L2 flush,
@@ -443,9 +447,54 @@ def kernel_suite(ops, dev, peak, steps, warmup, which=("snakebeta", "norms", "we
                                                   count=S, steps=S, guidance=1.5) for s in sets],
                4 * n * (2 * S + 2), set_bytes, note="latency-bound: 13 MB")
         del sets
+    # Rows next to the path.  Window assembly: 8 decoded 1000-frame windows of the render schedule
+    # (hop 750, overlap 250 frames; src/levo-renderer-pattern.cpp:137-203), finiteness check on.
+    if "assembly" in which:
+        nw, ws, hop, ov = 8, 1000 * 1920, 750 * 1920, 250 * 1920
+        target = (nw - 1) * hop + ws
+        win = torch.from_numpy(rng.standard_normal((nw, 2, ws), dtype=np.float32)).to(dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        nbytes = 4 * win.numel() + 4 * 2 * target  # every window sample read once (hop + overlap = window)
+        sets = [(win if i == 0 else win.clone(), torch.empty((2, target), dtype=torch.float32, device=dev))
+                for i in range(input_sets(nbytes))]
+        entry_(f"assemble_windows_f32[{nw},2,{ws}]",
+               [lambda s=s: ops.assemble_windows_t(s[0], hop, ov, target, out=s[1], status=status) for s in sets],
+               nbytes, nbytes)
+        del sets, win
+    # Latent hand-off: one 5-minute song's Flow latent [7500][64] de-normalised into the VAE layout
+    # (src/levo-flow-conditioning.cpp:125-135, src/levo-render.cpp:181-193).
+    if "latent" in which:
+        fr, dim = 7500, 64
+        lat = torch.from_numpy(rng.standard_normal((fr, dim), dtype=np.float32)).to(dev)
+        mean = torch.from_numpy(rng.standard_normal(dim, dtype=np.float32)).to(dev)
+        std = torch.from_numpy(rng.uniform(0.5, 2.0, dim).astype(np.float32)).to(dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        nbytes = 8 * lat.numel()
+        sets = [(lat.clone(), torch.empty((dim, fr), dtype=torch.float32, device=dev))
+                for _ in range(max(input_sets(nbytes), KERNEL_LAUNCHES))]
+        entry_(f"latent_to_vae_f32[{fr},{dim}]",
+               [lambda s=s: ops.latent_to_vae_t(s[0], mean, std, out=s[1], status=status) for s in sets],
+               nbytes, nbytes, note="latency-bound: 3.8 MB per launch")
+        del sets, lat
+    # Greedy next tokens: a serving batch of 64 requests x 3 codebook streams over the LeLM's 16384 codes
+    # + EOS (src/levo-model.h:109-111), with a 50-token repetition window and the penalty of
+    # src/levo-sampling.cpp:129-152.
+    if "greedy" in which:
+        rows, vocab = 64 * 3, 16385
+        logits = torch.from_numpy(rng.standard_normal((rows, vocab), dtype=np.float32)).to(dev)
+        recent = torch.from_numpy(rng.integers(0, vocab - 1, (rows, 50))).to(dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        nbytes = 4 * logits.numel() + 8 * recent.numel() + 8 * rows
+        sets = [(logits.clone(), torch.empty(rows, dtype=torch.int64, device=dev))
+                for _ in range(max(input_sets(nbytes), KERNEL_LAUNCHES))]
+        entry_(f"greedy_tokens_f32[{rows},{vocab}]",
+               [lambda s=s: ops.greedy_tokens_t(s[0], recent, penalty=1.1, penalty_limit=vocab - 1,
+                                                status=status, out=s[1]) for s in sets],
+               nbytes, nbytes, note="one CTA per row: 192 rows")
+        del sets, logits
     # What a plain device copy of the same byte count reaches at these sizes (torch, not ours), timed
     # the same way: the achievable ceiling for ~50 MB kernels, where ramp-up and drain are a large share.
-    for mb in (50, 496) if len(which) == 4 else (50,):
+    for mb in (50, 496) if "snakebeta" in which else (50,):
         src = torch.empty(mb * 1024 * 1024 // 8, dtype=torch.float32, device=dev)
         set_bytes = 2 * src.numel() * 4
         sets = [(src.clone(), torch.empty_like(src)) for _ in range(input_sets(set_bytes))]
@@ -626,7 +675,7 @@ def only_kernels(args):
     ops = entry.load_package().ops
     peak, _ = measured_peak()
     which = tuple(k.strip() for k in args.kernels.split(",") if k.strip())
-    unknown = set(which) - {"snakebeta", "norms", "weightnorm", "euler"}
+    unknown = set(which) - set(KERNEL_FAMILIES)
     if unknown:
         raise SystemExit(f"--kernels: unknown {sorted(unknown)}")
     emit({"kernels": kernel_suite(ops, dev, peak, steps=args.steps, warmup=args.warmup, which=which)})

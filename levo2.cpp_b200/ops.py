@@ -469,10 +469,12 @@ ASSEMBLE_STATUS_LIMIT = 1 << 30
 
 
 def assemble_windows_t(windows, hop_samples: int, overlap_samples: int, target_samples: int, interleaved=False,
-                       out=None, check_finite=True):
+                       out=None, check_finite=True, status=None):
     """Crossfade-assemble decoded windows [W, C, S] into [C, target] (or [target, C] interleaved).
     With check_finite (the reference's require_finite_audio) a non-finite sample in any window raises
-    LevoNonFinite with the reference's message for the first (window, channel), after a synchronize."""
+    LevoNonFinite with the reference's message for the first (window, channel), after a synchronize.
+    With a caller-owned status tensor (device int32, zeroed) the check runs but nothing is read back:
+    the caller decodes the word (LEVO_ASSEMBLE_STATUS) itself, and the call stays asynchronous."""
     import torch
 
     _require_cuda(windows, out)
@@ -480,11 +482,13 @@ def assemble_windows_t(windows, hop_samples: int, overlap_samples: int, target_s
     if out is None:
         shape = (target_samples, c) if interleaved else (c, target_samples)
         out = torch.empty(shape, dtype=torch.float32, device=windows.device)
-    status = torch.zeros(1, dtype=torch.int32, device=windows.device) if check_finite else None
+    own = status is None and check_finite
+    if own:
+        status = torch.zeros(1, dtype=torch.int32, device=windows.device)
     check(lib().levo_assemble_windows_f32(_ptr(windows), w, c, s, hop_samples, overlap_samples, target_samples,
                                           _ptr(out), 1 if interleaved else 0, _ptr(status),
                                           _stream(windows.device)))
-    word = int(status.item()) if status is not None else 0
+    word = int(status.item()) if own else 0
     if word:
         pair = ASSEMBLE_STATUS_LIMIT - word
         k, ch = divmod(pair, c)
@@ -514,18 +518,22 @@ def _raise_if_flagged(status, what: str, message: str) -> None:
         raise LevoNonFinite(ENONFINITE, f"{what}: {message}")
 
 
-def latent_to_vae_t(frame_major, mean=None, stddev=None, out=None, check_finite=True):
+def latent_to_vae_t(frame_major, mean=None, stddev=None, out=None, check_finite=True, status=None):
     """[frames, dim] frame-major (normalised) latent -> [dim, frames] de-normalised VAE input.  With
-    check_finite a non-finite input raises LevoNonFinite, as denormalize_latents throws."""
+    check_finite a non-finite input raises LevoNonFinite, as denormalize_latents throws; with a
+    caller-owned status tensor (device int32, zeroed) the flag is set there and not read back."""
     import torch
 
     _require_cuda(frame_major, mean, stddev, out)
     frames, dim = frame_major.shape
     out = torch.empty((dim, frames), dtype=torch.float32, device=frame_major.device) if out is None else out
-    status = torch.zeros(1, dtype=torch.int32, device=frame_major.device) if check_finite else None
+    own = status is None and check_finite
+    if own:
+        status = torch.zeros(1, dtype=torch.int32, device=frame_major.device)
     check(lib().levo_latent_to_vae_f32(_ptr(frame_major), _ptr(mean), _ptr(stddev), frames, dim, _ptr(out),
                                        _ptr(status), _stream(frame_major.device)))
-    _raise_if_flagged(status, "levo_latent_to_vae_f32", "normalized latent contains a non-finite value")
+    if own:
+        _raise_if_flagged(status, "levo_latent_to_vae_f32", "normalized latent contains a non-finite value")
     return out
 
 

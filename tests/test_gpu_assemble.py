@@ -108,3 +108,28 @@ def test_assembly_without_the_check_runs_through(ops, dev):
     w[1, 0, 9] = float("nan")
     out = ops.assemble_windows_t(w, 5, 5, 15, check_finite=False)
     assert torch.isnan(out[0, 14]).item()
+
+
+@pytest.mark.parametrize("interleaved", [False, True])
+@pytest.mark.parametrize("k,s", [(0, 17), (1, 19), (2, 18), (2, 3)])
+def test_assembly_vector_form_checks_samples_no_output_reads(ops, dev, interleaved, k, s):
+    """The same check on the four-samples-at-a-time form (every length a multiple of 4): 3 stereo windows
+    of 20 samples, hop 12, overlap 4, crop at 40: samples 16..19 of every window feed no output; sample 3
+    of the last one does."""
+    w = np.zeros((3, 2, 20), np.float32)
+    w[k, 0, s] = np.inf
+    with pytest.raises(ValueError, match=f"decoded left channel contains non-finite samples \\(window {k}\\)"):
+        ops.assemble_windows_t(torch.from_numpy(w).to(dev), 12, 4, 40, interleaved=interleaved)
+
+
+def test_assembly_vector_and_scalar_forms_agree(ops, orc, dev):
+    """An output tensor one float past a 16-byte boundary takes the scalar form; both forms give the
+    oracle's bits."""
+    rng = np.random.default_rng(41)
+    w = rng.standard_normal((4, 2, 64)).astype(np.float32)
+    tw = torch.from_numpy(w).to(dev)
+    want = orc.assemble_windows(w, 48, 16, 200)
+    vec = ops.assemble_windows_t(tw, 48, 16, 200).cpu().numpy()
+    buf = torch.empty(2 * 200 + 1, device=dev)
+    scalar = ops.assemble_windows_t(tw, 48, 16, 200, out=buf[1:].view(2, 200)).cpu().numpy()
+    assert np.array_equal(vec, want) and np.array_equal(scalar, want)
