@@ -33,6 +33,7 @@ struct GreedyArgs {
     int64_t n_ignore;
     int64_t *out;
     int32_t *status;
+    int vec;  // float4 scan after a scalar head to each row's 16-byte boundary
 };
 
 // a beats b: larger value, or equal value at a smaller index.
@@ -40,7 +41,7 @@ __device__ __forceinline__ bool better(float va, int64_t ia, float vb, int64_t i
     return va > vb || (va == vb && ia < ib);
 }
 
-__global__ void __launch_bounds__(kThreads) greedy_kernel(const GreedyArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) greedy_kernel(const GreedyArgs a) {
     extern __shared__ uint32_t bits[];  // [pen words][ign words]
     __shared__ float red_v[kThreads / 32];
     __shared__ int64_t red_i[kThreads / 32];
@@ -70,19 +71,61 @@ __global__ void __launch_bounds__(kThreads) greedy_kernel(const GreedyArgs a) {
         float best = -INFINITY;
         int64_t bidx = INT64_MAX;
         bool nan = false;
-        for (int64_t i = threadIdx.x; i < a.vocab; i += blockDim.x) {
-            float v = x[i];
-            const uint32_t m = 1u << (i & 31);
-            if (pen[i >> 5] & m) v = __fdiv_rn(v, a.penalty);
-            if (ign[i >> 5] & m) v = -INFINITY;
+        // one logit: penalty, ignore list, NaN flag, then the (value, smaller index) order
+        auto consider = [&](float v, int64_t i, uint32_t pbit, uint32_t ibit) {
+            if (pbit) v = __fdiv_rn(v, a.penalty);
+            if (ibit) v = -INFINITY;
             if (isnan(v)) {
                 nan = true;
-                continue;
+                return;
             }
             if (better(v, i, best, bidx)) {
                 best = v;
                 bidx = i;
             }
+        };
+        int64_t i0 = 0;  // first logit of the scalar tail
+        if (a.vec) {
+            // A scalar head up to the row's first 16-byte boundary, then four logits per float4 whose
+            // bitmap bits come from one 64-bit window of two words; the loads of a thread's groups go
+            // out before the comparisons.
+            const int64_t head = (4 - static_cast<int64_t>((reinterpret_cast<uintptr_t>(x) >> 2) & 3)) & 3;
+            if (threadIdx.x < head && threadIdx.x < a.vocab) {
+                const int64_t i = threadIdx.x;
+                const uint32_t m = 1u << (i & 31);
+                consider(x[i], i, pen[i >> 5] & m, ign[i >> 5] & m);
+            }
+            const int nv = static_cast<int>((a.vocab - head) / 4);
+            const float4 *x4 = reinterpret_cast<const float4 *>(x + head);
+            constexpr int kAhead = 4;
+            for (int g0 = threadIdx.x; g0 < nv; g0 += kAhead * kThreads) {
+                float4 q[kAhead];
+#pragma unroll
+                for (int j = 0; j < kAhead; ++j)
+                    if (g0 + j * kThreads < nv) q[j] = x4[g0 + j * kThreads];
+#pragma unroll
+                for (int j = 0; j < kAhead; ++j) {
+                    const int g = g0 + j * kThreads;
+                    if (g >= nv) break;
+                    const int64_t i = head + 4 * static_cast<int64_t>(g);
+                    const int64_t w = i >> 5;
+                    const int sh = static_cast<int>(i & 31);
+                    const bool two = w + 1 < words;
+                    const uint32_t pw = static_cast<uint32_t>(
+                        ((static_cast<uint64_t>(two ? pen[w + 1] : 0u) << 32) | pen[w]) >> sh);
+                    const uint32_t iw = static_cast<uint32_t>(
+                        ((static_cast<uint64_t>(two ? ign[w + 1] : 0u) << 32) | ign[w]) >> sh);
+                    consider(q[j].x, i, pw & 1u, iw & 1u);
+                    consider(q[j].y, i + 1, pw & 2u, iw & 2u);
+                    consider(q[j].z, i + 2, pw & 4u, iw & 4u);
+                    consider(q[j].w, i + 3, pw & 8u, iw & 8u);
+                }
+            }
+            i0 = head + 4 * static_cast<int64_t>(nv);
+        }
+        for (int64_t i = i0 + threadIdx.x; i < a.vocab; i += blockDim.x) {
+            const uint32_t m = 1u << (i & 31);
+            consider(x[i], i, pen[i >> 5] & m, ign[i >> 5] & m);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -143,8 +186,9 @@ LEVO_OPS_API int levo_greedy_tokens_f32(const float *logits, int64_t rows, int64
         if (ptrs[i] && !aligned_to(ptrs[i], align[i]))
             return set_error(LEVO_OPS_EINVAL, std::string(w) + ": pointer is not aligned to its element size");
     const int64_t limit = penalty_limit <= 0 ? vocab : std::min(penalty_limit, vocab);
+    const int vec = aligned_to(logits, 4) ? 1 : 0;  // each row finds its own 16-byte boundary
     const GreedyArgs a{logits, rows, vocab, ld, recent_len > 0 ? recent : nullptr, recent_len, penalty, limit,
-                       n_ignore > 0 ? ignore : nullptr, n_ignore, tokens_out, status};
+                       n_ignore > 0 ? ignore : nullptr, n_ignore, tokens_out, status, vec};
     const size_t smem = static_cast<size_t>(2 * ((vocab + 31) / 32)) * sizeof(uint32_t);
     const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * 4);
     greedy_kernel<<<static_cast<unsigned>(grid), kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a);
