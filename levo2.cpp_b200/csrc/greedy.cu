@@ -10,8 +10,10 @@
 //      depend on it.  A NaN logit is an error in the reference (:81); here it
 //      sets bit 0 (value 1) of the optional status word.
 // One CTA per stream row: the recent / ignored ids are marked in shared-memory
-// bitmaps, the row is scanned once with coalesced loads, and (value, index)
-// pairs are reduced with a first-index tie break, so the result is exact.
+// bitmaps, the row is scanned once (a scalar head up to its 16-byte boundary,
+// then float4 groups whose loads go out ahead of the comparisons), and
+// (value, index) pairs are reduced with a first-index tie break, a total order,
+// so the result is exact whatever the order of the comparisons.
 #include <algorithm>
 
 #include "common.cuh"
