@@ -41,6 +41,13 @@ __device__ __forceinline__ void note_sample(const AsmArgs &a, float v, int64_t k
         atomicMax(a.status, static_cast<int32_t>(LEVO_ASSEMBLE_STATUS(k * a.channels + c)));
 }
 
+// prev * (1 - alpha) + cur * alpha with alpha = s / (overlap - 1), rounded step by step as the
+// reference's crossfade does
+__device__ __forceinline__ float blend(float prev, float cur, int64_t s, float denom) {
+    const float alpha = __fdiv_rn(static_cast<float>(s), denom);
+    return __fadd_rn(__fmul_rn(prev, __fsub_rn(1.0f, alpha)), __fmul_rn(cur, alpha));
+}
+
 __device__ __forceinline__ float assembled_sample(const AsmArgs &a, int64_t c, int64_t t) {
     int64_t k = t / a.hop;
     if (k > a.windows - 1) k = a.windows - 1;
@@ -50,8 +57,7 @@ __device__ __forceinline__ float assembled_sample(const AsmArgs &a, int64_t c, i
     if (k == 0 || s >= a.overlap) return cur;
     const float prev = a.win[((k - 1) * a.channels + c) * a.window_samples + s + a.hop];
     note_sample(a, prev, k - 1, c);
-    const float alpha = __fdiv_rn(static_cast<float>(s), a.denom);
-    return __fadd_rn(__fmul_rn(prev, __fsub_rn(1.0f, alpha)), __fmul_rn(cur, alpha));
+    return blend(prev, cur, s, a.denom);
 }
 
 // Samples no output reads (past hop + overlap in every window but the last, and past the crop) are
@@ -93,11 +99,6 @@ __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast
 __device__ __forceinline__ void note4(const AsmArgs &a, const float4 &v, int64_t k, int64_t c) {
     if (a.status != nullptr && !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w)))
         atomicMax(a.status, static_cast<int32_t>(LEVO_ASSEMBLE_STATUS(k * a.channels + c)));
-}
-
-__device__ __forceinline__ float blend(float prev, float cur, int64_t s, float denom) {
-    const float alpha = __fdiv_rn(static_cast<float>(s), denom);
-    return __fadd_rn(__fmul_rn(prev, __fsub_rn(1.0f, alpha)), __fmul_rn(cur, alpha));
 }
 
 // Outputs t0..t0+3 of channel c (t0 % 4 == 0): with hop and overlap multiples of 4 the four share
